@@ -1,0 +1,761 @@
+"""Benchmark of the B200 operator library (one JSON line on rank 0).
+
+Headline workload ("row ops FP32"): one step is one pass
+of softmax 4096x1024 (x ~ N(0, 2^2)), RMSNorm 2048x4096 (x ~ N(0,1),
+w ~ N(1, 0.1), eps 1e-6) and transpose 4096x4096 (U[-1,1)), each through the
+C-ABI.  `value` is algorithmic HBM bytes moved per second over all ranks
+(GB/s), with inputs resident in HBM; `e2e` is the same metric with the step's
+inputs copied from pinned host memory and its outputs read back inside the
+timed region.  Buffers rotate over sets larger than L2 (126 MB) so every
+step streams from HBM.
+
+Extra lines of evidence go in `ops` (every other BASELINE config on this
+GPU count, including the sharded attention / GEMM workloads split across
+ranks) and `ref_b200` (the reference's own launchers built for sm_100a, same
+shapes, same GPU).
+
+--impl reference times the reference's CPU verification loops (compiled from
+its sources into oracle/_ref, else the C restatement in oracle/) on the host
+cores, on the same workload.
+
+Multi-GPU: launch under torchrun; one rank per GPU, NCCL for the barrier and
+the max-over-ranks timing.  Row ops and the headline are weak-scaled (each
+rank owns its own rows), the sharded configs strong-scaled.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO / "orin-cuda-operator-library_b200", REPO):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+L2_BYTES = 126 * 2**20
+
+SOFTMAX_SHAPE = (4096, 1024)
+RMS_SHAPE = (2048, 4096)
+TRANSPOSE_SHAPE = (4096, 4096)
+RMS_EPS = 1e-6
+# algorithmic bytes (reads + writes, each element once)
+SOFTMAX_BYTES = 2 * 4 * SOFTMAX_SHAPE[0] * SOFTMAX_SHAPE[1]
+RMS_BYTES = 2 * 4 * RMS_SHAPE[0] * RMS_SHAPE[1] + 4 * RMS_SHAPE[1]
+TRANSPOSE_BYTES = 2 * 4 * TRANSPOSE_SHAPE[0] * TRANSPOSE_SHAPE[1]
+STEP_BYTES = SOFTMAX_BYTES + RMS_BYTES + TRANSPOSE_BYTES
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description="operatorlib B200 benchmark")
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-extras", action="store_true",
+                   help="headline line only (skip the per-config ops table)")
+    p.add_argument("--only", default="",
+                   help="comma list of extra workloads to run (default all)")
+    return p.parse_args(argv)
+
+
+def load_peaks() -> dict:
+    try:
+        data = json.loads(PEAKS_FILE.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]),
+                "bf16_tflops": float(data["bf16_tflops"]),
+                "bf16_tflops_sustained": float(data.get("bf16_tflops_sustained",
+                                                        data["bf16_tflops"])),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+                "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------ distributed
+
+class Dist:
+    """Rank bookkeeping; NCCL process group when WORLD_SIZE > 1."""
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, backend="nccl"):
+        import torch
+        import torch.distributed as dist
+
+        if self.world > 1 and not dist.is_initialized():
+            if backend == "nccl":
+                torch.cuda.set_device(self.local_rank)
+            dist.init_process_group(backend=backend)
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg is not None:
+            import torch
+
+            if torch.cuda.is_available():
+                self.pg.barrier(device_ids=[self.local_rank])
+            else:
+                self.pg.barrier()
+
+    def max(self, value: float) -> float:
+        if self.pg is None:
+            return value
+        import torch
+
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        t = torch.tensor([value], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.destroy_process_group()
+
+
+def shard_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous, balanced split of `total` units: rank r gets
+    [begin, end) with sizes differing by at most one."""
+    base, extra = divmod(total, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+# ------------------------------------------------------------ clock sampling
+
+REASON_BITS = {  # NVML clocks-event-reason bits
+    "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+    "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+    "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+}
+
+
+class ClockSampler:
+    """Samples the SM clock and throttle reasons of this rank's GPU through
+    NVML every `period` seconds on a background thread (reading only)."""
+
+    def __init__(self, torch_device: int, period: float = 0.01):
+        self.period = period
+        self.samples: list[tuple[float, int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._handle = None
+        self._nvml = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            import torch
+
+            props = torch.cuda.get_device_properties(torch_device)
+            bus = "%08X:%02X:%02X.0" % (getattr(props, "pci_domain_id", 0),
+                                         props.pci_bus_id, props.pci_device_id)
+            self._handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            self._nvml = pynvml
+        except Exception as exc:  # no NVML: report it, never fake clocks
+            self.error = f"nvml unavailable: {exc}"
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((time.perf_counter(), mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self, t0: float | None = None, t1: float | None = None) -> dict:
+        if self._nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "note": getattr(self, "error", "nvml unavailable")}
+        window = [s for s in self.samples
+                  if (t0 is None or s[0] >= t0) and (t1 is None or s[0] <= t1)]
+        if not window:
+            window = self.samples
+        busy = [s for s in window if not (s[2] & REASON_BITS["gpu_idle"])] or window
+        mask = 0
+        for s in busy:
+            mask |= s[2]
+        reasons = [k for k, bit in REASON_BITS.items() if mask & bit and k != "gpu_idle"]
+        return {"sm_mhz": statistics.median(s[1] for s in busy) if busy else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(busy)}
+
+
+# ------------------------------------------------------------ timing helpers
+
+def timed_loop(step, steps: int, warmup: int, dist: Dist, stream, marks=None):
+    """Runs `warmup` untimed steps, then `steps` timed ones bracketed by a
+    barrier and device synchronisation, timed with CUDA events on `stream`.
+    Returns (ms_per_step max over ranks, host t0, host t1)."""
+    import torch
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    start.record(stream)
+    for i in range(steps):
+        step(warmup + i)
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / steps
+    return dist.max(ms), t0, t1
+
+
+# ------------------------------------------------------------ headline: row ops
+
+def gen_rowops(rng, rows_scale: int = 1):
+    """BASELINE configs[1] inputs (host, float32)."""
+    sm = rng.normal(0, 2, SOFTMAX_SHAPE).astype(np.float32)
+    rx = rng.normal(0, 1, RMS_SHAPE).astype(np.float32)
+    rw = rng.normal(1, 0.1, RMS_SHAPE[1]).astype(np.float32)
+    tx = rng.uniform(-1, 1, TRANSPOSE_SHAPE).astype(np.float32)
+    return sm, rx, rw, tx
+
+
+class RowOpsSet:
+    """One rotation set of device buffers for the headline step."""
+
+    def __init__(self, host, dev):
+        import torch
+
+        sm, rx, rw, tx = host
+        self.sm_in = torch.from_numpy(sm).to(dev)
+        self.sm_out = torch.empty_like(self.sm_in)
+        self.rx = torch.from_numpy(rx).to(dev)
+        self.rw = torch.from_numpy(rw).to(dev)
+        self.r_out = torch.empty_like(self.rx)
+        self.tx = torch.from_numpy(tx).to(dev)
+        self.t_out = torch.empty(TRANSPOSE_SHAPE[::-1], device=dev)
+
+
+def rowops_call(lib, s, stream_handle, events=None):
+    """The three C-ABI calls of one headline step; optional per-kernel events
+    (recorded on the launching stream) for the roofline."""
+    if events is not None:
+        events[0].record()
+    rc = lib.opl_softmax_f32(s.sm_in.data_ptr(), s.sm_out.data_ptr(),
+                             SOFTMAX_SHAPE[0], SOFTMAX_SHAPE[1], stream_handle)
+    if events is not None:
+        events[1].record()
+    rc |= lib.opl_rmsnorm_f32(s.rx.data_ptr(), s.rw.data_ptr(), s.r_out.data_ptr(),
+                              RMS_SHAPE[0], RMS_SHAPE[1], RMS_EPS, stream_handle)
+    if events is not None:
+        events[2].record()
+    rc |= lib.opl_transpose_f32(s.tx.data_ptr(), s.t_out.data_ptr(),
+                                TRANSPOSE_SHAPE[0], TRANSPOSE_SHAPE[1], stream_handle)
+    if events is not None:
+        events[3].record()
+    if rc != 0:
+        raise RuntimeError(f"row-op launch failed (code {rc})")
+
+
+def bench_rowops(args, dist, dev, peaks):
+    import torch
+
+    import operatorlib
+
+    lib = operatorlib.capi()
+    rng = np.random.default_rng(1000 + dist.rank)
+    host = gen_rowops(rng)
+    n_sets = max(2, -(-2 * L2_BYTES // STEP_BYTES) + 1)  # >= 2x L2 of traffic between reuses
+    sets = [RowOpsSet(host, dev) for _ in range(n_sets)]
+    stream = torch.cuda.current_stream(dev)
+    handle = stream.cuda_stream
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
+              for _ in range(args.steps)]
+
+    def step(i):
+        rec = events[i - args.warmup] if i >= args.warmup else None
+        rowops_call(lib, sets[i % n_sets], handle, rec)
+
+    ms, t0, t1 = timed_loop(step, args.steps, args.warmup, dist, stream)
+    per_kernel = {"softmax": 0.0, "rmsnorm": 0.0, "transpose": 0.0}
+    for ev in events:
+        per_kernel["softmax"] += ev[0].elapsed_time(ev[1])
+        per_kernel["rmsnorm"] += ev[1].elapsed_time(ev[2])
+        per_kernel["transpose"] += ev[2].elapsed_time(ev[3])
+    per_kernel = {k: v / args.steps for k, v in per_kernel.items()}
+    kernel_bytes = {"softmax": SOFTMAX_BYTES, "rmsnorm": RMS_BYTES,
+                    "transpose": TRANSPOSE_BYTES}
+
+    # sanity: last outputs are right (cheap spot checks, outside the timing)
+    s = sets[(args.warmup + args.steps - 1) % n_sets]
+    torch.cuda.synchronize()
+    assert torch.equal(s.t_out[:7, :5], s.tx[:5, :7].t())
+    got = s.sm_out[:3].double().sum(dim=1)
+    assert torch.allclose(got, torch.ones_like(got), atol=1e-4)
+
+    # e2e: pinned host inputs -> device -> ops -> pinned host outputs.
+    pin = [torch.from_numpy(a).pin_memory() for a in host]
+    pin_out = [torch.empty(SOFTMAX_SHAPE).pin_memory(), torch.empty(RMS_SHAPE).pin_memory(),
+               torch.empty(TRANSPOSE_SHAPE[::-1]).pin_memory()]
+    h2d = sum(t.numel() * 4 for t in pin)
+    d2h = sum(t.numel() * 4 for t in pin_out)
+
+    def e2e_step(i):
+        st = sets[i % n_sets]
+        st.sm_in.copy_(pin[0], non_blocking=True)
+        st.rx.copy_(pin[1], non_blocking=True)
+        st.rw.copy_(pin[2], non_blocking=True)
+        st.tx.copy_(pin[3], non_blocking=True)
+        rowops_call(lib, st, handle)
+        pin_out[0].copy_(st.sm_out, non_blocking=True)
+        pin_out[1].copy_(st.r_out, non_blocking=True)
+        pin_out[2].copy_(st.t_out, non_blocking=True)
+
+    e2e_ms, _, _ = timed_loop(e2e_step, args.steps, min(args.warmup, 3), dist, stream)
+    dominant = max(per_kernel, key=per_kernel.get)
+    dom_ms = dist.max(per_kernel[dominant])
+    achieved = kernel_bytes[dominant] / (dom_ms * 1e-3) / 1e9
+    return {
+        "ms": ms, "t0": t0, "t1": t1, "e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h,
+        "per_kernel_ms": {k: round(v, 5) for k, v in per_kernel.items()},
+        "per_kernel_gbs": {k: round(kernel_bytes[k] / (per_kernel[k] * 1e-3) / 1e9, 1)
+                           for k in per_kernel},
+        "dominant": dominant, "dominant_gbs": achieved,
+        "dominant_bytes": kernel_bytes[dominant], "n_sets": n_sets,
+    }
+
+
+# ------------------------------------------------------------ other configs
+
+def _rotations(bytes_per_set: int) -> int:
+    return max(1, min(8, -(-2 * L2_BYTES // max(bytes_per_set, 1)) + 1))
+
+
+def _measure(call, steps, warmup, dist, stream):
+    ms, _, _ = timed_loop(call, steps, warmup, dist, stream)
+    return ms
+
+
+def extras(args, dist, dev, peaks, only: set[str]):
+    """Every BASELINE config besides the headline; returns {name: record}.
+    Row ops / reduce: weak-scaled per rank.  'attn_sharded' and
+    'gemm_sharded': strong-scaled, units split contiguously across ranks."""
+    import torch
+
+    import operatorlib
+
+    lib = operatorlib.capi()
+    stream = torch.cuda.current_stream(dev)
+    h = stream.cuda_stream
+    rng = np.random.default_rng(77 + dist.rank)
+    steps = max(3, min(args.steps, 20))
+    warm = max(3, min(args.warmup, 5))
+    hbm = peaks["hbm_gbs"]
+    tc = peaks["bf16_tflops"]
+    ffma = 148 * 128 * 2 * 1.965e9 / 1e12  # FP32 FFMA spec peak, TFLOP/s
+    out = {}
+
+    def want(name):
+        return not only or name in only
+
+    def record(name, ms, work, bound, peak, unit, note=None, world_units=1):
+        scale = 1e9 if unit == "GB/s" else 1e12
+        rate = work * world_units / (ms * 1e-3) / scale
+        r = {"ms": round(ms, 5), "value": round(rate, 3), "unit": unit,
+             "bound": bound, "frac_per_gpu": round(rate / world_units / peak, 4)}
+        if note:
+            r["note"] = note
+        out[name] = r
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    # reduce: N = 16,777,216 per rank (weak); partial in FP64 + NCCL all-reduce
+    if want("reduce"):
+        n = 16_777_216
+        xs = [t(rng.uniform(-1, 1, n).astype(np.float32)) for _ in range(_rotations(4 * n))]
+        part = torch.empty((), dtype=torch.float64, device=dev)
+        res = torch.empty((), device=dev)
+
+        def call(i):
+            if dist.world == 1:
+                assert lib.opl_reduce_sum_f32(xs[i % len(xs)].data_ptr(), res.data_ptr(), n, h) == 0
+            else:
+                assert lib.opl_reduce_sum_partial_f64(xs[i % len(xs)].data_ptr(), part.data_ptr(), n, h) == 0
+                dist.pg.all_reduce(part)
+        ms = _measure(call, steps, warm, dist, stream)
+        record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world)
+
+    # ragged row ops 4097x1023
+    if want("ragged"):
+        r, c = 4097, 1023
+        x = [t(rng.normal(0, 2, (r, c)).astype(np.float32)) for _ in range(_rotations(8 * r * c))]
+        y = torch.empty((r, c), device=dev)
+        yt = torch.empty((c, r), device=dev)
+        w = t(rng.normal(1, 0.1, c).astype(np.float32))
+        ms = _measure(lambda i: lib.opl_softmax_f32(x[i % len(x)].data_ptr(), y.data_ptr(), r, c, h), steps, warm, dist, stream)
+        record("softmax_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
+        ms = _measure(lambda i: lib.opl_rmsnorm_f32(x[i % len(x)].data_ptr(), w.data_ptr(), y.data_ptr(), r, c, RMS_EPS, h), steps, warm, dist, stream)
+        record("rmsnorm_4097x1023", ms, 8 * r * c + 4 * c, "hbm", hbm, "GB/s", world_units=dist.world)
+        ms = _measure(lambda i: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
+        record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
+
+    # GEMM 4096^3 FP16 (tensor cores), FP32 (FFMA), non-aligned FP16
+    for name, dtype, (m, n, k) in [("gemm_f16_4096", np.float16, (4096, 4096, 4096)),
+                                   ("gemm_f16_4095x4097x4093", np.float16, (4095, 4097, 4093)),
+                                   ("gemm_f32_4096", np.float32, (4096, 4096, 4096))]:
+        if not want(name.rsplit("_", 1)[0]) and not want(name):
+            continue
+        a = t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dtype))
+        b = t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype))
+        cc = torch.empty((m, n), device=dev)
+        fn = lib.opl_gemm_f16 if dtype == np.float16 else lib.opl_gemm_f32
+        ms = _measure(lambda i: fn(a.data_ptr(), b.data_ptr(), cc.data_ptr(), m, n, k, h),
+                      max(3, steps // 2), warm, dist, stream)
+        peak = tc if dtype == np.float16 else ffma
+        record(name, ms, 2.0 * m * n * k, "tensor" if dtype == np.float16 else "ffma",
+               peak, "TFLOP/s", world_units=dist.world)
+
+    # attention B1 H12 S1024 D128, FP16 and FP32, causal and not
+    for dtype in (np.float16, np.float32):
+        tag = "f16" if dtype == np.float16 else "f32"
+        if not want(f"attention_{tag}"):
+            continue
+        shape = (1, 12, 1024, 128)
+        q, k_, v = (t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+        o = torch.empty(shape, device=dev)
+        fn = lib.opl_attention_f16 if tag == "f16" else lib.opl_attention_f32
+        for causal in (0, 1):
+            ms = _measure(lambda i: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                       1, 12, 1024, 128, causal, h), steps, warm, dist, stream)
+            flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
+            record(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops,
+                   "tensor" if tag == "f16" else "ffma", tc if tag == "f16" else ffma,
+                   "TFLOP/s", note="causal-exact FLOPs" if causal else None,
+                   world_units=dist.world)
+
+    # sharded causal attention B8 H32 S4096 D128 (strong scaling over B*H)
+    if want("attn_sharded"):
+        total_heads, s_len, d = 8 * 32, 4096, 128
+        b0, b1 = shard_range(total_heads, dist.world, dist.rank)
+        mine = b1 - b0
+        q, k_, v = (t(rng.normal(0, 1, (mine, s_len, d)).astype(np.float16)) for _ in range(3))
+        o = torch.empty((mine, s_len, d), device=dev)
+        ms = _measure(lambda i: lib.opl_attention_f16(q.data_ptr(), k_.data_ptr(), v.data_ptr(),
+                                                      o.data_ptr(), 1, mine, s_len, d, 1, h),
+                      max(3, steps // 4), 2, dist, stream)
+        flops = 2.0 * total_heads * d * s_len * (s_len + 1)
+        rate = flops / (ms * 1e-3) / 1e12
+        out["attn_sharded_b8h32s4096d128_causal"] = {
+            "ms": round(ms, 4), "value": round(rate, 2), "unit": "TFLOP/s", "bound": "tensor",
+            "frac_per_gpu": round(rate / dist.world / tc, 4), "scaling": "strong",
+            "heads_per_rank": mine, "note": "causal-exact FLOPs; dense-count = 2x"}
+        del q, k_, v, o
+
+    # sharded FP16 GEMM 16384^3 (strong scaling over M row blocks, B replicated)
+    if want("gemm_sharded"):
+        M = N = K = 16384
+        m0, m1 = shard_range(M, dist.world, dist.rank)
+        a = t((rng.uniform(-1, 1, (m1 - m0, K)) / np.sqrt(K)).astype(np.float16))
+        b = t((rng.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(np.float16))
+        cc = torch.empty((m1 - m0, N), device=dev)
+        ms = _measure(lambda i: lib.opl_gemm_f16(a.data_ptr(), b.data_ptr(), cc.data_ptr(),
+                                                 m1 - m0, N, K, h), 3, 1, dist, stream)
+        rate = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        out["gemm_sharded_f16_16384"] = {
+            "ms": round(ms, 4), "value": round(rate, 2), "unit": "TFLOP/s", "bound": "tensor",
+            "frac_per_gpu": round(rate / dist.world / tc, 4), "scaling": "strong",
+            "rows_per_rank": m1 - m0}
+        del a, b, cc
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------ reference on B200
+
+def ref_b200(args, dist, dev, peaks):
+    """The reference's own launchers (its src/*.cu built for sm_100a into
+    oracle/_ref) on the same shapes and GPU: the "reference on B200" column.
+    Timing evidence only; returns {} when oracle/_ref is absent."""
+    import torch
+
+    from oracle import oracle as orc
+
+    ref = orc.ref_gpu()
+    if ref is None:
+        return {"unavailable": "oracle/_ref/libref_operatorlib.so not built"}
+    stream = torch.cuda.current_stream(dev)
+    h = stream.cuda_stream
+    rng = np.random.default_rng(5)
+    steps, warm = max(3, min(args.steps, 10)), 3
+    res = {}
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    def rate(name, ms, work, unit):
+        scale = 1e9 if unit == "GB/s" else 1e12
+        res[name] = {"ms": round(ms, 4), "value": round(work / (ms * 1e-3) / scale, 3), "unit": unit}
+
+    host = gen_rowops(rng)
+    sets = [RowOpsSet(host, dev) for _ in range(3)]
+    ms = _measure(lambda i: ref.ref_softmax_f32(sets[i % 3].sm_in.data_ptr(), sets[i % 3].sm_out.data_ptr(), *SOFTMAX_SHAPE, h), steps, warm, dist, stream)
+    rate("softmax_4096x1024", ms, SOFTMAX_BYTES, "GB/s")
+    ms = _measure(lambda i: ref.ref_rmsnorm_f32(sets[i % 3].rx.data_ptr(), sets[i % 3].rw.data_ptr(), sets[i % 3].r_out.data_ptr(), *RMS_SHAPE, RMS_EPS, h), steps, warm, dist, stream)
+    rate("rmsnorm_2048x4096", ms, RMS_BYTES, "GB/s")
+    ms = _measure(lambda i: ref.ref_transpose_f32(sets[i % 3].tx.data_ptr(), sets[i % 3].t_out.data_ptr(), *TRANSPOSE_SHAPE, h), steps, warm, dist, stream)
+    rate("transpose_4096x4096", ms, TRANSPOSE_BYTES, "GB/s")
+    del sets
+    n = 16_777_216
+    xs = [t(rng.uniform(-1, 1, n).astype(np.float32)) for _ in range(5)]
+    r = torch.empty((), device=dev)
+    ms = _measure(lambda i: ref.ref_reduce_sum_f32(xs[i % 5].data_ptr(), r.data_ptr(), n, h), steps, warm, dist, stream)
+    rate("reduce_16M", ms, 4 * n, "GB/s")
+    del xs
+    for dtype, fn, tag in [(np.float16, ref.ref_gemm_f16, "gemm_f16_4096"),
+                           (np.float32, ref.ref_gemm_f32, "gemm_f32_4096")]:
+        a = t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype))
+        b = t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype))
+        c = torch.empty((4096, 4096), device=dev)
+        ms = _measure(lambda i: fn(a.data_ptr(), b.data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), 3, 1, dist, stream)
+        rate(tag, ms, 2.0 * 4096**3, "TFLOP/s")
+    shape = (1, 12, 1024, 128)
+    for dtype, fn, tag in [(np.float16, ref.ref_attention_f16, "f16"),
+                           (np.float32, ref.ref_attention_f32, "f32")]:
+        q, k_, v = (t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+        o = torch.empty(shape, device=dev)
+        for causal in (0, 1):
+            ms = _measure(lambda i: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 12, 1024, 128, causal, h), 3, 1, dist, stream)
+            flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
+            rate(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops, "TFLOP/s")
+    torch.cuda.empty_cache()
+    return res
+
+
+# ------------------------------------------------------------ CPU baseline
+
+class CpuRowOps:
+    """The reference's CPU loops (oracle/_ref, kind "reference") or the C
+    restatement (oracle/, kind "port") over the headline workload, rows split
+    across `threads` host threads (ctypes releases the GIL)."""
+
+    def __init__(self, threads: int):
+        from oracle import oracle as orc
+
+        self.orc = orc
+        self.ref = orc.ref_cpu()
+        self.kind = "reference" if self.ref is not None else "port"
+        self.threads = max(1, threads)
+        rng = np.random.default_rng(4242)
+        self.sm, self.rx, self.rw, self.tx = gen_rowops(rng)
+        self.sm_out = np.empty_like(self.sm)
+        self.r_out = np.empty_like(self.rx)
+        self.t_out = np.empty(TRANSPOSE_SHAPE[::-1], dtype=np.float32)
+        from concurrent.futures import ThreadPoolExecutor
+
+        self.pool = ThreadPoolExecutor(self.threads)
+
+    def _split(self, rows):
+        return [shard_range(rows, self.threads, i) for i in range(self.threads)]
+
+    def step(self):
+        F = self.orc._fp
+        L = self.ref if self.ref is not None else self.orc.lib()
+        soft = L.ref_cpu_softmax if self.ref is not None else L.oracle_softmax
+        rms = L.ref_cpu_rmsnorm if self.ref is not None else L.oracle_rmsnorm
+        tra = L.ref_cpu_transpose if self.ref is not None else L.oracle_transpose
+        cols = SOFTMAX_SHAPE[1]
+        jobs = []
+        for r0, r1 in self._split(SOFTMAX_SHAPE[0]):
+            jobs.append(self.pool.submit(soft, F(self.sm[r0:]), F(self.sm_out[r0:]), r1 - r0, cols))
+        hid = RMS_SHAPE[1]
+        for r0, r1 in self._split(RMS_SHAPE[0]):
+            jobs.append(self.pool.submit(rms, F(self.rx[r0:]), F(self.rw), F(self.r_out[r0:]),
+                                         r1 - r0, hid, RMS_EPS))
+        rows, tcols = TRANSPOSE_SHAPE
+
+        def tpart(r0, r1):
+            tmp = np.empty((tcols, r1 - r0), dtype=np.float32)
+            tra(F(self.tx[r0:]), F(tmp), r1 - r0, tcols)
+            self.t_out[:, r0:r1] = tmp
+        for r0, r1 in self._split(rows):
+            jobs.append(self.pool.submit(tpart, r0, r1))
+        for j in jobs:
+            j.result()
+
+    def measure(self, budget_s: float, max_steps: int, min_steps: int = 1):
+        times = []
+        t_start = time.perf_counter()
+        while len(times) < max_steps:
+            t0 = time.perf_counter()
+            self.step()
+            times.append(time.perf_counter() - t0)
+            if len(times) >= min_steps and time.perf_counter() - t_start > budget_s:
+                break
+        return times
+
+
+def cpu_baseline_record() -> dict:
+    from oracle import oracle as orc
+
+    cpu = CpuRowOps(orc.cpu_threads())
+    cpu.step()  # warm caches / page in
+    times = cpu.measure(budget_s=10.0, max_steps=200)
+    sec = statistics.median(times)
+    return {"value": round(STEP_BYTES / sec / 1e9, 3), "unit": "GB/s",
+            "cores": cpu.threads, "kind": cpu.kind,
+            "sample": f"{len(times)} full steps of the headline workload "
+                      f"(softmax 4096x1024 + rmsnorm 2048x4096 + transpose 4096^2), "
+                      f"median step {sec * 1e3:.1f} ms, rows split over {cpu.threads} threads"}
+
+
+# ------------------------------------------------------------ main
+
+def committed_traffic(kernel: str):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/dram_traffic.json), or None."""
+    try:
+        data = json.loads((REPO / "profiles" / "dram_traffic.json").read_text())
+        return data[kernel]["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
+def run_reference(args, dist) -> int:
+    if dist.rank != 0:
+        return 0
+    from oracle import oracle as orc
+
+    cpu = CpuRowOps(orc.cpu_threads())
+    for _ in range(max(args.warmup, 0)):
+        cpu.step()
+    times = cpu.measure(budget_s=float("inf"), max_steps=args.steps, min_steps=args.steps)
+    sec = sum(times) / len(times)
+    value = STEP_BYTES / sec / 1e9
+    line = {
+        "metric": "row-op HBM GB/s (softmax+rmsnorm+transpose, BASELINE configs[1])",
+        "value": round(value, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "rowops_f32: softmax 4096x1024 + rmsnorm 2048x4096 "
+                               "+ transpose 4096x4096", "device": "host CPU"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cpu.threads,
+                         "kind": cpu.kind,
+                         "sample": f"{args.steps} full workload steps after {args.warmup} warm-up"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, dist) -> int:
+    import torch
+
+    import operatorlib
+
+    operatorlib.capi()  # fail loudly if the CUDA library is missing
+    dist.init("nccl")
+    dev = torch.device("cuda", dist.local_rank)
+    torch.cuda.set_device(dev)
+    peaks = load_peaks()
+    only = {s for s in args.only.split(",") if s}
+    with ClockSampler(dist.local_rank) as clocks:
+        head = bench_rowops(args, dist, dev, peaks)
+        ops = {} if args.no_extras else extras(args, dist, dev, peaks, only)
+        ref = ref_b200(args, dist, dev, peaks) if (dist.world == 1 and not args.no_extras
+                                                   and not only) else None
+    code = ctypes_int = None
+    import ctypes
+
+    ctypes_int = ctypes.c_int(0)
+    code = operatorlib.capi().opl_read_and_clear_watchdog(ctypes_int)
+    watchdog = ctypes_int.value if code == 0 else f"read failed ({code})"
+    cpu = cpu_baseline_record() if (dist.rank == 0 and dist.world == 1) else None
+    if dist.rank == 0:
+        value = STEP_BYTES * dist.world / (head["ms"] * 1e-3) / 1e9
+        e2e = STEP_BYTES * dist.world / (head["e2e_ms"] * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        line = {
+            "metric": "row-op HBM GB/s (softmax+rmsnorm+transpose, BASELINE configs[1])",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(head["ms"], 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {
+                "workload": "rowops_f32: softmax 4096x1024 N(0,4) + rmsnorm 2048x4096 "
+                            "N(0,1), w N(1,0.01), eps 1e-6 + transpose 4096x4096 U[-1,1)",
+                "per_rank": "each rank owns its own full row set (row-sharded, no collective)",
+                "l2": f"inputs rotate over {head['n_sets']} buffer sets "
+                      f"({head['n_sets'] * STEP_BYTES / 2**20:.0f} MiB > 2x L2)",
+                "algorithmic_bytes_per_step_per_rank": STEP_BYTES,
+            },
+            "e2e": {"value": round(e2e, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"],
+                    "path": "C-ABI calls with pinned-host H2D of inputs and D2H of outputs"},
+            "roofline": {"bound": "hbm", "kernel": head["dominant"],
+                         "achieved": round(head["dominant_gbs"], 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(head["dominant_gbs"] / peak, 4),
+                         "traffic": committed_traffic(head["dominant"]),
+                         "algorithmic_bytes": head["dominant_bytes"],
+                         "peak_source": f"{peaks['source']} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
+                         if peaks["source"] == "measured" else "fallback 6.65 TB/s"},
+            "per_kernel_gbs": head["per_kernel_gbs"],
+            "per_kernel_ms": head["per_kernel_ms"],
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks.summary(head["t0"], head["t1"]),
+            "watchdog": watchdog,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if ops:
+            line["ops"] = ops
+        if ref is not None:
+            line["ref_b200"] = ref
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.close()
+    return 0
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    dist = Dist()
+    if args.impl == "reference":
+        return run_reference(args, dist)
+    return run_ours(args, dist)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,14 @@
+// Internal interface of the SIMT (FFMA) GEMM.
+#pragma once
+
+#include "opl_common.cuh"
+
+namespace opl {
+
+// Row-major C[M,N] = A[M,K] * B[K,N] with FP32 FFMA accumulation; T is float
+// or __half (converted to FP32 on load).  Any shape and alignment.
+template <typename T>
+cudaError_t gemm_simt(const T* a, const T* b, float* c, int m, int n, int k,
+                      cudaStream_t stream);
+
+}  // namespace opl

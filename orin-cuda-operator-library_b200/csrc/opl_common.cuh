@@ -1,0 +1,77 @@
+// Shared device/host helpers for the sm_100a operator kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cstddef>
+#include <cstdint>
+
+#include "operatorlib/opl_capi.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "operatorlib-b200 kernels are written for sm_100a only"
+#endif
+
+namespace opl {
+
+constexpr unsigned kFullMask = 0xffffffffu;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFullMask, v, o));
+  return v;
+}
+
+// Streaming 128-bit load that does not allocate in L1 (inputs are read once).
+__device__ __forceinline__ float4 ld_stream(const float4* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float ld_stream(const float* p) {
+  float r;
+  asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(r) : "l"(p));
+  return r;
+}
+
+// Streaming stores: outputs are written once and not re-read by the kernel.
+__device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
+__device__ __forceinline__ void st_stream(float* p, float v) { __stcs(p, v); }
+
+// Kernels with bounded spin-waits write a non-zero code into the per-device
+// watchdog word when a wait gives up (see opl_read_and_clear_watchdog); the
+// word's device address comes from watchdog_word() and is a kernel argument.
+__device__ __forceinline__ void watchdog_trip(int* word, int code) {
+  atomicCAS(word, 0, code);
+}
+
+// Device address of the current device's watchdog word (nullptr on error).
+int* watchdog_word();
+
+// Number of SMs of the current device, cached per device (thread-safe).
+int sm_count();
+// Current device ordinal (cudaGetDevice), -1 on failure.
+int current_device();
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
+}
+
+}  // namespace opl

@@ -1,0 +1,137 @@
+"""Parity of GEMM and attention on the GPU through the C-ABI.
+
+Oracles: the exact double GEMM product and the reference's double attention
+loop restated in oracle/opl_oracle.c (pinned in test_oracle_pins.py).
+Gates: FP16 GEMM / attention max-abs <= 2e-2 and rel <= 1e-2 against the
+FP64 reference; FP32 GEMM 1e-3 + 1e-3*|ref| (reference
+tests/gemm_smoke.cu:76); FP32 attention atol = rtol = 1e-4 (reference
+tests/attention_smoke.cu:108).  FP16 inputs are quantised to half before the
+oracle sees them, as the reference does (attention_fp16_common.h:15-22).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import operatorlib
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(a, cuda):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+
+
+def run_gemm(cuda, stream, a, b):
+    import torch
+
+    c = torch.empty((a.shape[0], b.shape[1]), device=cuda)
+    operatorlib.gemm_into(dev(a, cuda), dev(b, cuda), c)
+    stream.synchronize()
+    return c.cpu().numpy()
+
+
+def check_f16(got, want):
+    err = np.abs(got.astype(np.float64) - want)
+    assert err.max() <= 2e-2, err.max()
+    assert np.all(err <= 2e-2 * np.abs(want) + 2e-2)
+    fro = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+    assert fro <= 1e-2, fro
+
+
+GEMM_F16 = [(128, 128, 32), (16, 128, 32), (32, 32, 32), (37, 65, 71),  # ref tests
+            (17, 19, 23), (1, 256, 64), (1, 1, 1), (128, 256, 64), (256, 512, 1024),
+            (1000, 1000, 1000), (512, 4096, 4096), (4095, 4097, 4093),
+            (4096, 4096, 4096), (300, 520, 136), (129, 257, 72)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_F16)
+def test_gemm_f16(cuda, stream, m, n, k):
+    rng = np.random.default_rng(m * 31 + n * 7 + k)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float16)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16)
+    got = run_gemm(cuda, stream, a, b)
+    if m * n * k <= 2**31:
+        want = orc.gemm(a.astype(np.float32), b.astype(np.float32), threads=8)
+        check_f16(got, want)
+    else:  # sample 96 rows spread over M for the big shapes
+        idx = np.unique(np.linspace(0, m - 1, 96).astype(int))
+        want = a[idx].astype(np.float64) @ b.astype(np.float64)
+        check_f16(got[idx], want)
+
+
+GEMM_F32 = [(1, 256, 64), (16, 128, 64), (128, 64, 32), (37, 65, 71),  # ref tests
+            (7, 37, 23), (128, 128, 8), (1, 1, 1), (513, 257, 129),
+            (1024, 1024, 1024), (4095, 4097, 4093)]
+
+
+@pytest.mark.parametrize("m,n,k", GEMM_F32)
+def test_gemm_f32(cuda, stream, m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    a = rng.uniform(-0.25, 0.25, (m, k)).astype(np.float32)
+    b = rng.uniform(-0.25, 0.25, (k, n)).astype(np.float32)
+    got = run_gemm(cuda, stream, a, b)
+    if m * n * k <= 2**31:
+        want = orc.gemm(a, b, threads=8)
+        np.testing.assert_allclose(got, want, rtol=1e-3, atol=1e-3)
+    else:
+        idx = np.unique(np.linspace(0, m - 1, 64).astype(int))
+        want = a[idx].astype(np.float64) @ b.astype(np.float64)
+        np.testing.assert_allclose(got[idx], want, rtol=1e-3, atol=1e-3)
+
+
+def run_attention(cuda, stream, q, k, v, causal):
+    import torch
+
+    o = torch.empty(q.shape, device=cuda)
+    operatorlib.attention_into(dev(q, cuda), dev(k, cuda), dev(v, cuda), o, causal)
+    stream.synchronize()
+    return o.cpu().numpy()
+
+
+ATT_CASES = [  # (B, H, S, D, causal, qk range)
+    (1, 2, 32, 64, False, 1.0), (1, 2, 32, 128, True, 1.0),  # reference tests
+    (1, 2, 37, 71, True, 20.0),                              # "extreme"
+    (1, 1, 1, 1, False, 1.0), (2, 3, 17, 16, True, 1.0), (1, 2, 128, 128, False, 1.0),
+    (1, 2, 200, 128, True, 1.0), (1, 4, 256, 64, True, 1.0), (2, 2, 513, 96, False, 1.0),
+    (1, 12, 1024, 128, False, None), (1, 12, 1024, 128, True, None),  # BASELINE
+]
+
+
+def att_inputs(shape, qk, seed, dtype):
+    rng = np.random.default_rng(seed)
+    if qk is None:  # BASELINE: Q/K/V ~ N(0,1)
+        q, k, v = (rng.normal(0, 1, shape) for _ in range(3))
+    else:
+        q = rng.uniform(-qk, qk, shape)
+        k = rng.uniform(-qk, qk, shape)
+        v = rng.uniform(-1, 1, shape)
+    return [x.astype(dtype) for x in (q, k, v)]
+
+
+@pytest.mark.parametrize("b,h,s,d,causal,qk", ATT_CASES)
+def test_attention_f16(cuda, stream, b, h, s, d, causal, qk):
+    q, k, v = att_inputs((b, h, s, d), qk, s * 3 + d, np.float16)
+    got = run_attention(cuda, stream, q, k, v, causal)
+    want = orc.attention(q.astype(np.float32), k.astype(np.float32),
+                         v.astype(np.float32), causal)
+    check_f16(got, want)
+
+
+@pytest.mark.parametrize("b,h,s,d,causal,qk", ATT_CASES[:9])
+def test_attention_f32(cuda, stream, b, h, s, d, causal, qk):
+    q, k, v = att_inputs((b, h, s, d), qk, s * 5 + d, np.float32)
+    got = run_attention(cuda, stream, q, k, v, causal)
+    want = orc.attention(q, k, v, causal)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+def test_attention_f32_baseline_shape_sampled_heads(cuda, stream):
+    q, k, v = att_inputs((1, 12, 1024, 128), None, 77, np.float32)
+    for causal in (False, True):
+        got = run_attention(cuda, stream, q, k, v, causal)
+        want = orc.attention(q[:, :2], k[:, :2], v[:, :2], causal)
+        np.testing.assert_allclose(got[:, :2], want, rtol=1e-4, atol=1e-4)
