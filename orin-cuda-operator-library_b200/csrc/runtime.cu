@@ -132,3 +132,50 @@ cudaError_t attention_f16(const __half* q, const __half* k, const __half* v,
 }
 
 }  // namespace operatorlib
+
+// ---------------------------------------------------------------- TMA maps
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tmap.cuh"
+
+namespace opl {
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+}  // namespace
+
+cudaError_t encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank,
+                        const void* base, const uint64_t* dims,
+                        const uint64_t* strides_bytes, const uint32_t* box,
+                        CUtensorMapSwizzle swizzle) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault,
+                                &status) == cudaSuccess &&
+        status == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return cudaErrorNotSupported;
+  cuuint64_t gdim[3];
+  cuuint64_t gstride[2];
+  cuuint32_t boxdim[3];
+  cuuint32_t estride[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    boxdim[i] = box[i];
+    if (i + 1 < rank) gstride[i] = strides_bytes[i];
+  }
+  const CUresult r = g_encode(map, dtype, static_cast<cuuint32_t>(rank),
+                              const_cast<void*>(base), gdim, gstride, boxdim, estride,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+}  // namespace opl
