@@ -7,9 +7,8 @@ extern "C" int opl_gemm_f16(const opl_half_t* a, const opl_half_t* b, float* c,
                             int m, int n, int k, opl_stream_t stream) {
   if (a == nullptr || b == nullptr || c == nullptr || m <= 0 || n <= 0 || k <= 0)
     return cudaErrorInvalidValue;
-  return opl::gemm_simt<__half>(reinterpret_cast<const __half*>(a),
-                                reinterpret_cast<const __half*>(b), c, m, n, k,
-                                stream);
+  return opl::gemm_f16_tc(reinterpret_cast<const __half*>(a),
+                          reinterpret_cast<const __half*>(b), c, m, n, k, stream);
 }
 
 extern "C" int opl_attention_f16(const opl_half_t* q, const opl_half_t* k,

@@ -11,4 +11,9 @@ template <typename T>
 cudaError_t gemm_simt(const T* a, const T* b, float* c, int m, int n, int k,
                       cudaStream_t stream);
 
+// Tensor-core (tcgen05) FP16 GEMM with FP32 accumulation and output; any
+// shape (unaligned strides are staged through padded copies).
+cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n,
+                        int k, cudaStream_t stream);
+
 }  // namespace opl

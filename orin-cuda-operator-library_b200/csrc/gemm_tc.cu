@@ -1,0 +1,322 @@
+// FP16 x FP16 -> FP32 GEMM on the 5th-generation tensor cores (tcgen05),
+// row-major C[M,N] = A[M,K] * B[K,N] (reference src/gemm.cu:230-336 and
+// :455-479 -- there a 128x128 WMMA tile kernel with cp.async).
+//
+// Persistent, warp-specialised kernel, one CTA per SM (192 threads):
+//   warp 0  TMA producer: per 64-wide K block, one 128x64 A box (K-major)
+//           and four 64x64 B boxes (N-major) into a 4-stage ring of 48 KB
+//           stages, 128-byte swizzled, completion on a "full" mbarrier;
+//   warp 1  MMA issuer (one thread): 4 x tcgen05.mma kind::f16
+//           M=128 N=256 K=16 per K block into a TMEM accumulator; commits
+//           release the smem stage ("empty") and, after the last K block,
+//           hand the accumulator to the epilogue ("tmem_full");
+//   warps 2-5 epilogue: tcgen05.ld of their 32 TMEM lanes (one C row per
+//           thread), predicated FP32 stores, then "tmem_empty".
+// The 512 TMEM columns hold two 128x256 FP32 accumulators, so the epilogue of
+// tile i overlaps the main loop of tile i+1.  Tiles are walked in groups of
+// 16 M blocks so concurrently running CTAs share A and B panels in L2.
+// B is consumed in its natural row-major (N-major) layout through the
+// descriptor's MN-major mode: no transposed copy.
+//
+// Every mbarrier wait is bounded (tc_common.cuh): a wait that gives up sets
+// the CTA's abort flag and the device watchdog word; the CTA then drains its
+// outstanding TMA loads and MMAs (again bounded), frees TMEM and exits.
+#include "gemm_simt.cuh"
+#include "tc_common.cuh"
+#include "tmap.cuh"
+
+namespace opl {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK * 2;       // 16 KB
+constexpr int kBBoxBytes = kBK * 64 * 2;     // 8 KB: 64 K rows x 64 N
+constexpr int kBBytes = kBBoxBytes * (kBN / 64);
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kGroupM = 16;
+constexpr uint32_t kIdesc = tc::idesc_f16_f32(kBM, kBN, false, true);
+constexpr size_t kSmemBytes = kStages * kStageBytes + 1024 + 256;
+
+struct Barriers {
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct TileGrid {
+  int m_blocks, n_blocks, tiles;
+  __device__ void coords(int t, int& mb, int& nb) const {
+    const int per_group = kGroupM * n_blocks;
+    const int group = t / per_group;
+    const int first_m = group * kGroupM;
+    const int rows = min(m_blocks - first_m, kGroupM);
+    const int local = t - group * per_group;
+    mb = first_m + local % rows;
+    nb = local / rows;
+  }
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
+                   const __grid_constant__ CUtensorMap map_b, float* __restrict__ c,
+                   int m, int n, int k, int ldc, int* watchdog) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  TileGrid grid;
+  grid.m_blocks = (m + kBM - 1) / kBM;
+  grid.n_blocks = (n + kBN - 1) / kBN;
+  grid.tiles = grid.m_blocks * grid.n_blocks;
+  const int k_blocks = (k + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      tc::mbar_init(&bars->full[s], 1);
+      tc::mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&bars->tmem_full[b], 1);
+      tc::mbar_init(&bars->tmem_empty[b], 128);
+    }
+    tc::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&map_a);
+    tc::prefetch_tmap(&map_b);
+  }
+  if (warp == 1) tc::tmem_alloc(&bars->tmem_base, kTmemCols);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    for (int t = blockIdx.x; t < grid.tiles && !*abort; t += gridDim.x) {
+      int mb, nb;
+      grid.coords(t, mb, nb);
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!tc::mbar_wait(&bars->empty[stage], phase ^ 1, abort, watchdog,
+                           tc::kWatchdogGemm))
+          break;
+        uint8_t* sa = smem + stage * kStageBytes;
+        uint8_t* sb = sa + kABytes;
+        tc::mbar_expect_tx(&bars->full[stage], kStageBytes);
+        tc::tma_load_2d(sa, &map_a, kb * kBK, mb * kBM, &bars->full[stage]);
+#pragma unroll
+        for (int j = 0; j < kBN / 64; ++j)
+          tc::tma_load_2d(sb + j * kBBoxBytes, &map_b, nb * kBN + j * 64, kb * kBK,
+                          &bars->full[stage]);
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (*abort) {  // let in-flight TMA writes land before the CTA exits
+      for (int s = 0; s < kStages; ++s)
+        if (issued_mask & (1u << s)) {
+          const uint32_t addr = tc::smem_u32(&bars->full[s]);
+          for (uint32_t i = 0; i < tc::kMaxPolls; ++i)
+            if (tc::mbar_try_wait(addr, (issued_parity >> s) & 1u)) break;
+        }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool issued_any = false;
+    for (int t = blockIdx.x; t < grid.tiles && !*abort; t += gridDim.x) {
+      if (!tc::mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1, abort, watchdog,
+                         tc::kWatchdogGemm))
+        break;
+      tc::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * kBN;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!tc::mbar_wait(&bars->full[stage], phase, abort, watchdog, tc::kWatchdogGemm))
+          break;
+        tc::tc_fence_after();
+        const uint32_t a_addr = tc::smem_u32(smem + stage * kStageBytes);
+        const uint32_t b_addr = a_addr + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // A: K-major rows of 128 B; a 16-wide K step is 32 B inside the
+          // swizzle atom.  B: N-major, 64-column boxes 8 KB apart; a 16-row
+          // K step is two 8-row groups (2 KB).
+          const uint64_t a_desc = tc::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+          const uint64_t b_desc = tc::smem_desc_sw128(b_addr + kk * 2048, kBBoxBytes, 1024);
+          tc::umma_f16(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0);
+        }
+        issued_any = true;
+        tc::umma_commit(&bars->empty[stage]);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (*abort) break;
+      tc::umma_commit(&bars->tmem_full[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (*abort && issued_any) {  // wait for issued MMAs before TMEM is freed
+      tc::umma_commit(&bars->drain);
+      const uint32_t addr = tc::smem_u32(&bars->drain);
+      for (uint32_t i = 0; i < tc::kMaxPolls; ++i)
+        if (tc::mbar_try_wait(addr, 0)) break;
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    const int row_in_tile = quarter * 32 + lane;
+    const bool vec_ok = (ldc % 4 == 0) && aligned16(c);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < grid.tiles; t += gridDim.x) {
+      if (!tc::mbar_wait(&bars->tmem_full[acc], acc_phase, abort, watchdog,
+                         tc::kWatchdogGemm))
+        break;
+      tc::tc_fence_after();
+      int mb, nb;
+      grid.coords(t, mb, nb);
+      const int row = mb * kBM + row_in_tile;
+      float* crow = c + static_cast<size_t>(row) * ldc;
+#pragma unroll 1
+      for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+        float v[32];
+        tc::tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                          acc * kBN + chunk * 32,
+                      v);
+        const int col = nb * kBN + chunk * 32;
+        if (row < m && col < n) {
+          if (vec_ok && col + 32 <= n) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              st_stream(reinterpret_cast<float4*>(crow + col + i),
+                        make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col + i < n) crow[col + i] = v[i];
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bars->tmem_empty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// Zero-padded copy of a rows x cols FP16 matrix into a prow x pcol buffer
+// (pcol a multiple of 8 so every row starts 16-byte aligned for TMA).
+__global__ void pad_half_kernel(const __half* __restrict__ src, int rows, int cols,
+                                __half* __restrict__ dst, int prow, int pcol) {
+  const size_t total = static_cast<size_t>(prow) * pcol;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / pcol);
+    const int col = static_cast<int>(i - static_cast<size_t>(r) * pcol);
+    dst[i] = (r < rows && col < cols) ? src[static_cast<size_t>(r) * cols + col]
+                                      : __float2half(0.0f);
+  }
+}
+
+cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, int n,
+                           int k, int lda, int ldb, int ldc, cudaStream_t stream) {
+  CUtensorMap map_a, map_b;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(lda) * 2};
+    const uint32_t box[2] = {kBK, kBM};
+    cudaError_t e = encode_tmap(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, dims,
+                                strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e != cudaSuccess) return e;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(ldb), static_cast<uint64_t>(k)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldb) * 2};
+    const uint32_t box[2] = {64, kBK};
+    cudaError_t e = encode_tmap(&map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, dims,
+                                strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e != cudaSuccess) return e;
+  }
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kSmemBytes));
+  if (e != cudaSuccess) return e;
+  const long long tiles =
+      static_cast<long long>((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
+  const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  gemm_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, c, m, n, k, ldc,
+                                                         watchdog_word());
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// Tensor-core GEMM for any shape: strides that TMA cannot address (rows not
+// a multiple of 16 bytes, or unaligned bases) go through zero-padded copies
+// in a stream-ordered workspace.
+cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
+                        cudaStream_t stream) {
+  const bool a_ok = (k % 8 == 0) && aligned16(a);
+  const bool b_ok = (n % 8 == 0) && (k % 8 == 0) && aligned16(b);
+  if (a_ok && b_ok) return launch_gemm_tc(a, b, c, m, n, k, k, n, n, stream);
+
+  const int kp = (k + 7) & ~7;
+  const int np = b_ok ? n : ((n + 7) & ~7);
+  const size_t a_elems = a_ok ? 0 : static_cast<size_t>(m) * kp;
+  const size_t b_elems = b_ok ? 0 : static_cast<size_t>(kp) * np;
+  const size_t a_bytes = (a_elems * 2 + 255) & ~size_t(255);
+  void* ws = nullptr;
+  cudaError_t e = cudaMallocAsync(&ws, a_bytes + b_elems * 2 + 16, stream);
+  if (e != cudaSuccess) return e;
+  __half* a_use = const_cast<__half*>(a);
+  __half* b_use = const_cast<__half*>(b);
+  const int threads = 256;
+  const int blocks = sm_count() * 8;
+  if (!a_ok) {
+    a_use = static_cast<__half*>(ws);
+    pad_half_kernel<<<blocks, threads, 0, stream>>>(a, m, k, a_use, m, kp);
+  }
+  if (!b_ok) {
+    b_use = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + a_bytes);
+    pad_half_kernel<<<blocks, threads, 0, stream>>>(b, k, n, b_use, kp, np);
+  }
+  e = cudaGetLastError();
+  if (e == cudaSuccess)
+    e = launch_gemm_tc(a_use, b_use, c, m, n, kp, a_ok ? k : kp, b_ok ? n : np, n, stream);
+  const cudaError_t f = cudaFreeAsync(ws, stream);
+  return e != cudaSuccess ? e : f;
+}
+
+}  // namespace opl

@@ -70,7 +70,7 @@ int sm_count();
 // Current device ordinal (cudaGetDevice), -1 on failure.
 int current_device();
 
-inline bool aligned16(const void* p) {
+__host__ __device__ inline bool aligned16(const void* p) {
   return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
 }
 
