@@ -64,6 +64,8 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-extras", action="store_true",
                    help="headline line only (skip the per-config ops table)")
+    p.add_argument("--no-cpu", action="store_true",
+                   help="skip the CPU-baseline leg (profiling runs)")
     p.add_argument("--only", default="",
                    help="comma list of extra workloads to run (default all)")
     return p.parse_args(argv)
@@ -702,7 +704,8 @@ def run_ours(args, dist) -> int:
     ctypes_int = ctypes.c_int(0)
     code = operatorlib.capi().opl_read_and_clear_watchdog(ctypes_int)
     watchdog = ctypes_int.value if code == 0 else f"read failed ({code})"
-    cpu = cpu_baseline_record() if (dist.rank == 0 and dist.world == 1) else None
+    cpu = (cpu_baseline_record() if (dist.rank == 0 and dist.world == 1 and not args.no_cpu)
+           else None)
     if dist.rank == 0:
         value = STEP_BYTES * dist.world / (head["ms"] * 1e-3) / 1e9
         e2e = STEP_BYTES * dist.world / (head["e2e_ms"] * 1e-3) / 1e9

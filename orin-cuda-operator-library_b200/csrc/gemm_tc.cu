@@ -237,16 +237,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Zero-padded copy of a rows x cols FP16 matrix into a prow x pcol buffer
-// (pcol a multiple of 8 so every row starts 16-byte aligned for TMA).
-__global__ void pad_half_kernel(const __half* __restrict__ src, int rows, int cols,
-                                __half* __restrict__ dst, int prow, int pcol) {
-  const size_t total = static_cast<size_t>(prow) * pcol;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(i / pcol);
-    const int col = static_cast<int>(i - static_cast<size_t>(r) * pcol);
-    dst[i] = (r < rows && col < cols) ? src[static_cast<size_t>(r) * cols + col]
-                                      : __float2half(0.0f);
+// (pcol a multiple of 8 so every row starts 16-byte aligned for TMA).  One
+// CTA row-strides over destination rows; each thread assembles 8 halves and
+// writes them as one 16-byte store.
+__global__ void __launch_bounds__(256)
+    pad_half_kernel(const __half* __restrict__ src, int rows, int cols,
+                    __half* __restrict__ dst, int prow, int pcol) {
+  const int groups = pcol / 8;
+  for (int r = blockIdx.x; r < prow; r += gridDim.x) {
+    const __half* srow = src + static_cast<size_t>(r) * cols;
+    uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+      __align__(16) __half v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int col = g * 8 + i;
+        v[i] = (r < rows && col < cols) ? srow[col] : __float2half(0.0f);
+      }
+      drow[g] = *reinterpret_cast<const uint4*>(v);
+    }
   }
 }
 
@@ -302,15 +311,13 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
   if (e != cudaSuccess) return e;
   __half* a_use = const_cast<__half*>(a);
   __half* b_use = const_cast<__half*>(b);
-  const int threads = 256;
-  const int blocks = sm_count() * 8;
   if (!a_ok) {
     a_use = static_cast<__half*>(ws);
-    pad_half_kernel<<<blocks, threads, 0, stream>>>(a, m, k, a_use, m, kp);
+    pad_half_kernel<<<m < 65535 ? m : 65535, 256, 0, stream>>>(a, m, k, a_use, m, kp);
   }
   if (!b_ok) {
     b_use = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + a_bytes);
-    pad_half_kernel<<<blocks, threads, 0, stream>>>(b, k, n, b_use, kp, np);
+    pad_half_kernel<<<kp < 65535 ? kp : 65535, 256, 0, stream>>>(b, k, n, b_use, kp, np);
   }
   e = cudaGetLastError();
   if (e == cudaSuccess)
