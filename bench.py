@@ -241,6 +241,33 @@ def timed_loop(step, steps: int, warmup: int, dist: Dist, stream, marks=None):
     return dist.max(ms), t0, t1
 
 
+def capture(fn):
+    """Captures fn(stream_handle) -- a sequence of C-ABI launches -- into a
+    CUDA graph so replays run back to back on the GPU without per-launch
+    host overhead (kernels here last only 5-30 us)."""
+    import torch
+
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn(side.cuda_stream)  # eager warm-up (attribute set-up, pools)
+    side.synchronize()
+    with torch.cuda.graph(g):
+        fn(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return g
+
+
+def graph_ms_per_launch(fn, launches: int, reps: int, dist, stream) -> float:
+    """Average device time of one launch: `launches` back-to-back launches
+    (fn(i, handle) enqueues launch i) captured in one graph, replayed `reps`
+    times after one warm replay, timed with CUDA events on `stream`."""
+    g = capture(lambda h: [fn(i, h) for i in range(launches)])
+    ms, _, _ = timed_loop(lambda i: g.replay(), reps, 1, dist, stream)
+    return ms / launches
+
+
 # ------------------------------------------------------------ headline: row ops
 
 def gen_rowops(rng, rows_scale: int = 1):
@@ -301,20 +328,30 @@ def bench_rowops(args, dist, dev, peaks):
     sets = [RowOpsSet(host, dev) for _ in range(n_sets)]
     stream = torch.cuda.current_stream(dev)
     handle = stream.cuda_stream
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(4)]
-              for _ in range(args.steps)]
+    # One CUDA graph per rotation set holds one step (three C-ABI launches);
+    # the timed loop replays them in turn.
+    graphs = [capture(lambda h, st=st: rowops_call(lib, st, h)) for st in sets]
 
     def step(i):
-        rec = events[i - args.warmup] if i >= args.warmup else None
-        rowops_call(lib, sets[i % n_sets], handle, rec)
+        graphs[i % n_sets].replay()
 
     ms, t0, t1 = timed_loop(step, args.steps, args.warmup, dist, stream)
-    per_kernel = {"softmax": 0.0, "rmsnorm": 0.0, "transpose": 0.0}
-    for ev in events:
-        per_kernel["softmax"] += ev[0].elapsed_time(ev[1])
-        per_kernel["rmsnorm"] += ev[1].elapsed_time(ev[2])
-        per_kernel["transpose"] += ev[2].elapsed_time(ev[3])
-    per_kernel = {k: v / args.steps for k, v in per_kernel.items()}
+    # Per-kernel average launch time: each op alone, back to back over the
+    # rotation sets, in one graph.
+    launches = 4 * n_sets
+    per_kernel = {
+        "softmax": graph_ms_per_launch(
+            lambda i, h: lib.opl_softmax_f32(sets[i % n_sets].sm_in.data_ptr(), sets[i % n_sets].sm_out.data_ptr(),
+                                             SOFTMAX_SHAPE[0], SOFTMAX_SHAPE[1], h), launches, args.steps, dist, stream),
+        "rmsnorm": graph_ms_per_launch(
+            lambda i, h: lib.opl_rmsnorm_f32(sets[i % n_sets].rx.data_ptr(), sets[i % n_sets].rw.data_ptr(),
+                                             sets[i % n_sets].r_out.data_ptr(), RMS_SHAPE[0], RMS_SHAPE[1],
+                                             RMS_EPS, h), launches, args.steps, dist, stream),
+        "transpose": graph_ms_per_launch(
+            lambda i, h: lib.opl_transpose_f32(sets[i % n_sets].tx.data_ptr(), sets[i % n_sets].t_out.data_ptr(),
+                                               TRANSPOSE_SHAPE[0], TRANSPOSE_SHAPE[1], h), launches, args.steps,
+            dist, stream),
+    }
     kernel_bytes = {"softmax": SOFTMAX_BYTES, "rmsnorm": RMS_BYTES,
                     "transpose": TRANSPOSE_BYTES}
 
@@ -363,9 +400,18 @@ def _rotations(bytes_per_set: int) -> int:
     return max(1, min(8, -(-2 * L2_BYTES // max(bytes_per_set, 1)) + 1))
 
 
-def _measure(call, steps, warmup, dist, stream):
-    ms, _, _ = timed_loop(call, steps, warmup, dist, stream)
-    return ms
+def _measure(call, steps, warmup, dist, stream, graph=True):
+    """Average time of call(i) (one launch, C-ABI return code checked).
+    graph=True replays `steps` launches captured in a CUDA graph; False
+    launches eagerly (paths with host-side collectives)."""
+    def checked(i, h=None):
+        rc = call(i) if h is None else call(i, h)
+        if rc not in (None, 0):
+            raise RuntimeError(f"launch failed with code {rc}")
+    if not graph:
+        ms, _, _ = timed_loop(checked, steps, warmup, dist, stream)
+        return ms
+    return graph_ms_per_launch(lambda i, h: checked(i, h), steps, max(3, warmup), dist, stream)
 
 
 def extras(args, dist, dev, peaks, only: set[str]):
@@ -409,13 +455,14 @@ def extras(args, dist, dev, peaks, only: set[str]):
         part = torch.empty((), dtype=torch.float64, device=dev)
         res = torch.empty((), device=dev)
 
-        def call(i):
-            if dist.world == 1:
-                assert lib.opl_reduce_sum_f32(xs[i % len(xs)].data_ptr(), res.data_ptr(), n, h) == 0
-            else:
+        if dist.world == 1:
+            ms = _measure(lambda i, hh: lib.opl_reduce_sum_f32(xs[i % len(xs)].data_ptr(), res.data_ptr(), n, hh),
+                          steps, warm, dist, stream)
+        else:  # local FP64 partial + NCCL all-reduce (eager launches)
+            def call(i):
                 assert lib.opl_reduce_sum_partial_f64(xs[i % len(xs)].data_ptr(), part.data_ptr(), n, h) == 0
                 dist.pg.all_reduce(part)
-        ms = _measure(call, steps, warm, dist, stream)
+            ms = _measure(call, steps, warm, dist, stream, graph=False)
         record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world)
 
     # ragged row ops 4097x1023
@@ -425,11 +472,11 @@ def extras(args, dist, dev, peaks, only: set[str]):
         y = torch.empty((r, c), device=dev)
         yt = torch.empty((c, r), device=dev)
         w = t(rng.normal(1, 0.1, c).astype(np.float32))
-        ms = _measure(lambda i: lib.opl_softmax_f32(x[i % len(x)].data_ptr(), y.data_ptr(), r, c, h), steps, warm, dist, stream)
+        ms = _measure(lambda i, h: lib.opl_softmax_f32(x[i % len(x)].data_ptr(), y.data_ptr(), r, c, h), steps, warm, dist, stream)
         record("softmax_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
-        ms = _measure(lambda i: lib.opl_rmsnorm_f32(x[i % len(x)].data_ptr(), w.data_ptr(), y.data_ptr(), r, c, RMS_EPS, h), steps, warm, dist, stream)
+        ms = _measure(lambda i, h: lib.opl_rmsnorm_f32(x[i % len(x)].data_ptr(), w.data_ptr(), y.data_ptr(), r, c, RMS_EPS, h), steps, warm, dist, stream)
         record("rmsnorm_4097x1023", ms, 8 * r * c + 4 * c, "hbm", hbm, "GB/s", world_units=dist.world)
-        ms = _measure(lambda i: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
+        ms = _measure(lambda i, h: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
         record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
 
     # GEMM 4096^3 FP16 (tensor cores), FP32 (FFMA), non-aligned FP16
@@ -442,7 +489,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         b = t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype))
         cc = torch.empty((m, n), device=dev)
         fn = lib.opl_gemm_f16 if dtype == np.float16 else lib.opl_gemm_f32
-        ms = _measure(lambda i: fn(a.data_ptr(), b.data_ptr(), cc.data_ptr(), m, n, k, h),
+        ms = _measure(lambda i, h: fn(a.data_ptr(), b.data_ptr(), cc.data_ptr(), m, n, k, h),
                       max(3, steps // 2), warm, dist, stream)
         peak = tc if dtype == np.float16 else ffma
         record(name, ms, 2.0 * m * n * k, "tensor" if dtype == np.float16 else "ffma",
@@ -458,7 +505,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         o = torch.empty(shape, device=dev)
         fn = lib.opl_attention_f16 if tag == "f16" else lib.opl_attention_f32
         for causal in (0, 1):
-            ms = _measure(lambda i: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(),
+            ms = _measure(lambda i, h: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(),
                                        1, 12, 1024, 128, causal, h), steps, warm, dist, stream)
             flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
             record(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops,
@@ -473,7 +520,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         mine = b1 - b0
         q, k_, v = (t(rng.normal(0, 1, (mine, s_len, d)).astype(np.float16)) for _ in range(3))
         o = torch.empty((mine, s_len, d), device=dev)
-        ms = _measure(lambda i: lib.opl_attention_f16(q.data_ptr(), k_.data_ptr(), v.data_ptr(),
+        ms = _measure(lambda i, h: lib.opl_attention_f16(q.data_ptr(), k_.data_ptr(), v.data_ptr(),
                                                       o.data_ptr(), 1, mine, s_len, d, 1, h),
                       max(3, steps // 4), 2, dist, stream)
         flops = 2.0 * total_heads * d * s_len * (s_len + 1)
@@ -491,7 +538,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         a = t((rng.uniform(-1, 1, (m1 - m0, K)) / np.sqrt(K)).astype(np.float16))
         b = t((rng.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(np.float16))
         cc = torch.empty((m1 - m0, N), device=dev)
-        ms = _measure(lambda i: lib.opl_gemm_f16(a.data_ptr(), b.data_ptr(), cc.data_ptr(),
+        ms = _measure(lambda i, h: lib.opl_gemm_f16(a.data_ptr(), b.data_ptr(), cc.data_ptr(),
                                                  m1 - m0, N, K, h), 3, 1, dist, stream)
         rate = 2.0 * M * N * K / (ms * 1e-3) / 1e12
         out["gemm_sharded_f16_16384"] = {
@@ -531,17 +578,17 @@ def ref_b200(args, dist, dev, peaks):
 
     host = gen_rowops(rng)
     sets = [RowOpsSet(host, dev) for _ in range(3)]
-    ms = _measure(lambda i: ref.ref_softmax_f32(sets[i % 3].sm_in.data_ptr(), sets[i % 3].sm_out.data_ptr(), *SOFTMAX_SHAPE, h), steps, warm, dist, stream)
+    ms = _measure(lambda i, h: ref.ref_softmax_f32(sets[i % 3].sm_in.data_ptr(), sets[i % 3].sm_out.data_ptr(), *SOFTMAX_SHAPE, h), steps, warm, dist, stream)
     rate("softmax_4096x1024", ms, SOFTMAX_BYTES, "GB/s")
-    ms = _measure(lambda i: ref.ref_rmsnorm_f32(sets[i % 3].rx.data_ptr(), sets[i % 3].rw.data_ptr(), sets[i % 3].r_out.data_ptr(), *RMS_SHAPE, RMS_EPS, h), steps, warm, dist, stream)
+    ms = _measure(lambda i, h: ref.ref_rmsnorm_f32(sets[i % 3].rx.data_ptr(), sets[i % 3].rw.data_ptr(), sets[i % 3].r_out.data_ptr(), *RMS_SHAPE, RMS_EPS, h), steps, warm, dist, stream)
     rate("rmsnorm_2048x4096", ms, RMS_BYTES, "GB/s")
-    ms = _measure(lambda i: ref.ref_transpose_f32(sets[i % 3].tx.data_ptr(), sets[i % 3].t_out.data_ptr(), *TRANSPOSE_SHAPE, h), steps, warm, dist, stream)
+    ms = _measure(lambda i, h: ref.ref_transpose_f32(sets[i % 3].tx.data_ptr(), sets[i % 3].t_out.data_ptr(), *TRANSPOSE_SHAPE, h), steps, warm, dist, stream)
     rate("transpose_4096x4096", ms, TRANSPOSE_BYTES, "GB/s")
     del sets
     n = 16_777_216
     xs = [t(rng.uniform(-1, 1, n).astype(np.float32)) for _ in range(5)]
     r = torch.empty((), device=dev)
-    ms = _measure(lambda i: ref.ref_reduce_sum_f32(xs[i % 5].data_ptr(), r.data_ptr(), n, h), steps, warm, dist, stream)
+    ms = _measure(lambda i, h: ref.ref_reduce_sum_f32(xs[i % 5].data_ptr(), r.data_ptr(), n, h), steps, warm, dist, stream)
     rate("reduce_16M", ms, 4 * n, "GB/s")
     del xs
     for dtype, fn, tag in [(np.float16, ref.ref_gemm_f16, "gemm_f16_4096"),
@@ -549,7 +596,7 @@ def ref_b200(args, dist, dev, peaks):
         a = t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype))
         b = t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype))
         c = torch.empty((4096, 4096), device=dev)
-        ms = _measure(lambda i: fn(a.data_ptr(), b.data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), 3, 1, dist, stream)
+        ms = _measure(lambda i, h: fn(a.data_ptr(), b.data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), 3, 1, dist, stream)
         rate(tag, ms, 2.0 * 4096**3, "TFLOP/s")
     shape = (1, 12, 1024, 128)
     for dtype, fn, tag in [(np.float16, ref.ref_attention_f16, "f16"),
@@ -557,7 +604,7 @@ def ref_b200(args, dist, dev, peaks):
         q, k_, v = (t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
         o = torch.empty(shape, device=dev)
         for causal in (0, 1):
-            ms = _measure(lambda i: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 12, 1024, 128, causal, h), 3, 1, dist, stream)
+            ms = _measure(lambda i, h: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 12, 1024, 128, causal, h), 3, 1, dist, stream)
             flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
             rate(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops, "TFLOP/s")
     torch.cuda.empty_cache()
