@@ -45,6 +45,19 @@ int opl_reduce_sum_f32(const float* input, float* output, size_t n,
 int opl_reduce_sum_partial_f64(const float* input, double* output, size_t n,
                                opl_stream_t stream);
 
+/* No counterpart in the reference.  opl_reduce_sum_f32 without any
+ * allocation, for callers that may not call cudaMalloc/cudaMallocAsync (code
+ * inside allocator hooks or pool callbacks, frameworks that own all device
+ * memory, fixed memory budgets).  Partial sums go to a fixed file-scope
+ * device array of 4096 FP64 slots (32 KiB, held by every GPU that loads the
+ * library until exit); a call needing more slots (a device with more than
+ * 1024 SMs) returns cudaErrorInvalidValue.  The first call on each device
+ * looks the array up (cudaGetSymbolAddress) and must come before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race;
+ * serialise them on one stream.  Same result as opl_reduce_sum_f32. */
+int opl_reduce_sum_f32_noalloc(const float* input, float* output, size_t n,
+                               opl_stream_t stream);
+
 /* Replaces operatorlib::softmax_f32, operators.h:16-17 (src/softmax.cu:182-202). */
 int opl_softmax_f32(const float* input, float* output, int rows, int cols,
                     opl_stream_t stream);

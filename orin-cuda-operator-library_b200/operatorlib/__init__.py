@@ -43,6 +43,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
     sigs = {
         "opl_reduce_sum_f32": [vp, vp, sz, vp],
         "opl_reduce_sum_partial_f64": [vp, vp, sz, vp],
+        "opl_reduce_sum_f32_noalloc": [vp, vp, sz, vp],
         "opl_softmax_f32": [vp, vp, i, i, vp],
         "opl_transpose_f32": [vp, vp, i, i, vp],
         "opl_rmsnorm_f32": [vp, vp, vp, i, i, f, vp],
