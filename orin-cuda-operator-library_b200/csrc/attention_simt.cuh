@@ -12,4 +12,12 @@ cudaError_t attention_simt(const T* q, const T* k, const T* v, float* out,
                            int batch, int heads, int seq, int d, bool causal,
                            cudaStream_t stream);
 
+// tcgen05 FP16 attention (FP32 state and output) for head_dim 64 or 128 with
+// 16-byte aligned tensors; attention_tc_supported says whether it applies.
+bool attention_tc_supported(int head_dim, const void* q, const void* k, const void* v,
+                            const void* out);
+cudaError_t attention_f16_tc(const __half* q, const __half* k, const __half* v, float* out,
+                             int batch, int heads, int seq, int head_dim, bool causal,
+                             cudaStream_t stream);
+
 }  // namespace opl

@@ -19,6 +19,12 @@ extern "C" int opl_attention_f16(const opl_half_t* q, const opl_half_t* k,
       batch <= 0 || heads <= 0 || sequence <= 0 || head_dim <= 0 ||
       head_dim > 128)
     return cudaErrorInvalidValue;
+  const __half* qh = reinterpret_cast<const __half*>(q);
+  const __half* kh = reinterpret_cast<const __half*>(k);
+  const __half* vh = reinterpret_cast<const __half*>(v);
+  if (opl::attention_tc_supported(head_dim, q, k, v, output))
+    return opl::attention_f16_tc(qh, kh, vh, output, batch, heads, sequence, head_dim,
+                                 causal != 0, stream);
   return opl::attention_simt<__half>(
       reinterpret_cast<const __half*>(q), reinterpret_cast<const __half*>(k),
       reinterpret_cast<const __half*>(v), output, batch, heads, sequence,

@@ -195,8 +195,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < grid.tiles; t += gridDim.x) {
-      if (!tc::mbar_wait(&bars->tmem_full[acc], acc_phase, abort, watchdog,
-                         tc::kWatchdogGemm))
+      if (!tc::mbar_wait_warp(&bars->tmem_full[acc], acc_phase, abort, watchdog,
+                              tc::kWatchdogGemm))
         break;
       tc::tc_fence_after();
       int mb, nb;
