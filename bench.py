@@ -66,6 +66,12 @@ def parse_args(argv=None):
                    help="headline line only (skip the per-config ops table)")
     p.add_argument("--no-cpu", action="store_true",
                    help="skip the CPU-baseline leg (profiling runs)")
+    p.add_argument("--profile", default="",
+                   help="profiling driver: run one operator eagerly --warmup + --steps "
+                        "times and exit (reduce|softmax|rmsnorm|transpose|gemm_f16|"
+                        "gemm_f32|attention_f16|attention_f32)")
+    p.add_argument("--shape", default="",
+                   help="shape for --profile, e.g. 4096,4096,4096 or 1,12,1024,128,1")
     p.add_argument("--only", default="",
                    help="comma list of extra workloads to run (default all)")
     return p.parse_args(argv)
@@ -799,8 +805,69 @@ def run_ours(args, dist) -> int:
     return 0
 
 
+def run_profile(args) -> int:
+    """Small, self-contained eager launches of one operator for ncu captures."""
+    import torch
+
+    import operatorlib
+
+    lib = operatorlib.capi()
+    dev = torch.device("cuda", 0)
+    h = torch.cuda.current_stream(dev).cuda_stream
+    shape = [int(v) for v in args.shape.split(",") if v]
+    rng = np.random.default_rng(0)
+
+    def t(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+    op = args.profile
+    if op in ("gemm_f16", "gemm_f32"):
+        m, n, k = shape or (4096, 4096, 4096)
+        dt = np.float16 if op == "gemm_f16" else np.float32
+        a = t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dt))
+        b = t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dt))
+        c = torch.empty((m, n), device=dev)
+        fn = lib.opl_gemm_f16 if op == "gemm_f16" else lib.opl_gemm_f32
+        call = lambda: fn(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, h)
+    elif op in ("attention_f16", "attention_f32"):
+        bsz, hd, sq, d, causal = shape or (1, 12, 1024, 128, 0)
+        dt = np.float16 if op == "attention_f16" else np.float32
+        q, k_, v = (t(rng.normal(0, 1, (bsz, hd, sq, d)).astype(dt)) for _ in range(3))
+        o = torch.empty((bsz, hd, sq, d), device=dev)
+        fn = lib.opl_attention_f16 if op == "attention_f16" else lib.opl_attention_f32
+        call = lambda: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(),
+                          bsz, hd, sq, d, causal, h)
+    elif op == "reduce":
+        n = shape[0] if shape else 16_777_216
+        x = t(rng.uniform(-1, 1, n).astype(np.float32))
+        r = torch.empty((), device=dev)
+        call = lambda: lib.opl_reduce_sum_f32(x.data_ptr(), r.data_ptr(), n, h)
+    elif op in ("softmax", "rmsnorm", "transpose"):
+        rows, cols = shape or {"softmax": SOFTMAX_SHAPE, "rmsnorm": RMS_SHAPE,
+                               "transpose": TRANSPOSE_SHAPE}[op]
+        x = t(rng.normal(0, 1, (rows, cols)).astype(np.float32))
+        w = t(rng.normal(1, 0.1, cols).astype(np.float32))
+        y = torch.empty((rows, cols), device=dev)
+        call = {"softmax": lambda: lib.opl_softmax_f32(x.data_ptr(), y.data_ptr(), rows, cols, h),
+                "rmsnorm": lambda: lib.opl_rmsnorm_f32(x.data_ptr(), w.data_ptr(), y.data_ptr(),
+                                                       rows, cols, RMS_EPS, h),
+                "transpose": lambda: lib.opl_transpose_f32(x.data_ptr(), y.data_ptr(), rows,
+                                                           cols, h)}[op]
+    else:
+        raise SystemExit(f"unknown --profile op {op}")
+    for _ in range(args.warmup + args.steps):
+        rc = call()
+        if rc != 0:
+            raise SystemExit(f"{op} failed with code {rc}")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": op, "shape": shape, "launches": args.warmup + args.steps}))
+    return 0
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if args.profile:
+        return run_profile(args)
     dist = Dist()
     if args.impl == "reference":
         return run_reference(args, dist)
