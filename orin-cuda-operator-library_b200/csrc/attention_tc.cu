@@ -3,19 +3,23 @@
 // :486-507 -- there a 16x16 WMMA kernel with QK^T on one warp).
 //
 // One CTA = one (batch*head, 128-query tile); causal grids start with the
-// longest (bottom) tiles.  256 threads:
-//   warp 0    TMA producer: Q once; K_j and V_j (128 keys each) into a
-//             2-stage ring, all 128-byte swizzled boxes of 64 columns from a
+// longest (bottom) tiles.  384 threads:
+//   warp 0    TMA producer: Q once; K_j and V_j (128 keys each) into two
+//             2-slot rings with separate barriers (K_{j+1} streams in as soon
+//             as QK_{j-1} is done, independent of PV), all 128-byte swizzled boxes of 64 columns from a
 //             3-D [B*H, S, D] tensor map (rows past S read as zero);
 //   warp 1    MMA issuer (one thread):
 //               S_j = Q K_j^T   M128 N128 K=D  (both K-major)   -> TMEM S[j%2]
 //               O  += P_j V_j   M128 N=D K128  (P K-major, V N-major) -> TMEM O
 //             QK_{j+1} is issued before PV_j, so the next scores are computed
 //             while the softmax warps work on tile j;
-//   warps 4-7 softmax (thread = query row = TMEM lane): read S_j (128 fp32
-//             registers), mask (keys >= S, causal), running max in the log2
-//             domain, P = exp2(s - m) rounded to FP16 into a swizzled shared
-//             tile (the A operand of PV), row sum in FP32.  The running max
+//   warps 4-11 softmax, two warpgroups, each owning half the keys of every
+//             row (thread = query row = TMEM lane; 64 fp32 scores in
+//             registers): mask only on edge tiles (keys >= S, causal), row
+//             max exchanged between the groups in shared memory, running max
+//             in the log2 domain, P = exp2(s - m) rounded to FP16 into a
+//             swizzled shared tile (the A operand of PV), row sum in FP32
+//             (per group, added at the end).  The running max
 //             used for P is only moved when a row's maximum grows by more
 //             than 8 (a factor 256), so O in TMEM is rescaled rarely; P then
 //             stays <= 256, well inside FP16.  At the end O / l is stored.
@@ -34,7 +38,7 @@ namespace {
 
 constexpr int kRowsQ = 128;
 constexpr int kKeys = 128;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr int kSoftmaxWarp0 = 4;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -49,7 +53,8 @@ struct AttnCfg {
   static constexpr int kQOff = 0;
   static constexpr int kStageOff = kTileBytes;
   static constexpr int kPOff = kStageOff + 2 * kStageBytes;
-  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr int kXchgOff = kPOff + kPBytes;             // 3 x 256 floats
+  static constexpr int kBarOff = kXchgOff + 3 * 256 * 4;
   static constexpr size_t kSmem = kBarOff + 256 + 1024;
   static constexpr uint32_t kIdescQK = tc::idesc_f16_f32(kRowsQ, kKeys, false, false);
   static constexpr uint32_t kIdescPV = tc::idesc_f16_f32(kRowsQ, D, false, true);
@@ -57,8 +62,10 @@ struct AttnCfg {
 
 struct AttnBars {
   uint64_t q_full;
-  uint64_t kv_full[2];
-  uint64_t kv_empty[2];
+  uint64_t k_full[2];
+  uint64_t k_empty[2];
+  uint64_t v_full[2];
+  uint64_t v_empty[2];
   uint64_t s_full[2];
   uint64_t p_ready;
   uint64_t pv_done;
@@ -66,6 +73,10 @@ struct AttnBars {
   uint32_t tmem_base;
   int abort;
 };
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
 
 // K-major SW128 operand made of 64-column boxes of 128 rows: the 16-wide K
 // step kk lives in box kk/4 at byte offset 32*(kk%4).
@@ -99,11 +110,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(&bars->kv_full[i], 1);
-      tc::mbar_init(&bars->kv_empty[i], 1);
+      tc::mbar_init(&bars->k_full[i], 1);
+      tc::mbar_init(&bars->k_empty[i], 1);
+      tc::mbar_init(&bars->v_full[i], 1);
+      tc::mbar_init(&bars->v_empty[i], 1);
       tc::mbar_init(&bars->s_full[i], 1);
     }
-    tc::mbar_init(&bars->p_ready, 128);
+    tc::mbar_init(&bars->p_ready, 256);
     tc::mbar_init(&bars->pv_done, 1);
     tc::mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -121,40 +134,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------- producer
-    uint32_t issued_mask = 0, issued_parity = 0;
+    // K and V have separate slots and barriers: K_{j+1} only waits for
+    // QK_{j-1} to finish with its slot, V_{j+1} for PV_{j-1}.
+    uint32_t issued_mask = 0, issued_parity = 0;  // bit s: K slot s, bit 2+s: V slot s
     tc::mbar_expect_tx(&bars->q_full, Cfg::kTileBytes);
 #pragma unroll
     for (int b = 0; b < Cfg::kBoxes; ++b)
       tc::tma_load_3d(smem + Cfg::kQOff + b * Cfg::kBoxBytes, &map_q, b * 64, q0, bh,
                       &bars->q_full);
-    for (int j = 0; j < n_tiles; ++j) {
+    for (int j = 0; j < n_tiles && !*abort; ++j) {
       const int st = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      if (!tc::mbar_wait(&bars->kv_empty[st], ph ^ 1, abort, watchdog,
-                         tc::kWatchdogAttention))
-        break;
       uint8_t* ks = smem + Cfg::kStageOff + st * Cfg::kStageBytes;
       uint8_t* vs = ks + Cfg::kTileBytes;
-      tc::mbar_expect_tx(&bars->kv_full[st], Cfg::kStageBytes);
+      if (!tc::mbar_wait(&bars->k_empty[st], ph ^ 1, abort, watchdog, tc::kWatchdogAttention))
+        break;
+      tc::mbar_expect_tx(&bars->k_full[st], Cfg::kTileBytes);
 #pragma unroll
-      for (int b = 0; b < Cfg::kBoxes; ++b) {
+      for (int b = 0; b < Cfg::kBoxes; ++b)
         tc::tma_load_3d(ks + b * Cfg::kBoxBytes, &map_k, b * 64, j * kKeys, bh,
-                        &bars->kv_full[st]);
-        tc::tma_load_3d(vs + b * Cfg::kBoxBytes, &map_v, b * 64, j * kKeys, bh,
-                        &bars->kv_full[st]);
-      }
+                        &bars->k_full[st]);
       issued_mask |= 1u << st;
       issued_parity = (issued_parity & ~(1u << st)) | (ph << st);
+      if (!tc::mbar_wait(&bars->v_empty[st], ph ^ 1, abort, watchdog, tc::kWatchdogAttention))
+        break;
+      tc::mbar_expect_tx(&bars->v_full[st], Cfg::kTileBytes);
+#pragma unroll
+      for (int b = 0; b < Cfg::kBoxes; ++b)
+        tc::tma_load_3d(vs + b * Cfg::kBoxBytes, &map_v, b * 64, j * kKeys, bh,
+                        &bars->v_full[st]);
+      issued_mask |= 4u << st;
+      issued_parity = (issued_parity & ~(4u << st)) | (ph << (st + 2));
     }
     if (*abort) {
       const uint32_t qa = tc::smem_u32(&bars->q_full);
       for (uint32_t i = 0; i < tc::kMaxPolls && !tc::mbar_try_wait(qa, 0); ++i) {
       }
-      for (int s = 0; s < 2; ++s)
-        if (issued_mask & (1u << s)) {
-          const uint32_t a = tc::smem_u32(&bars->kv_full[s]);
+      for (int b = 0; b < 4; ++b)
+        if (issued_mask & (1u << b)) {
+          const uint32_t a = tc::smem_u32(b < 2 ? &bars->k_full[b] : &bars->v_full[b - 2]);
           for (uint32_t i = 0; i < tc::kMaxPolls; ++i)
-            if (tc::mbar_try_wait(a, (issued_parity >> s) & 1u)) break;
+            if (tc::mbar_try_wait(a, (issued_parity >> b) & 1u)) break;
         }
     }
   } else if (warp == 1 && lane == 0) {
@@ -164,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t p_addr = tc::smem_u32(smem + Cfg::kPOff);
     auto issue_qk = [&](int j) -> bool {
       const int st = j & 1;
-      if (!tc::mbar_wait(&bars->kv_full[st], (j >> 1) & 1, abort, watchdog,
+      if (!tc::mbar_wait(&bars->k_full[st], (j >> 1) & 1, abort, watchdog,
                          tc::kWatchdogAttention))
         return false;
       tc::tc_fence_after();
@@ -174,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::umma_f16(tmem + st * kKeys, kmajor_desc(q_addr, kk, Cfg::kBoxBytes),
                      kmajor_desc(k_addr, kk, Cfg::kBoxBytes), Cfg::kIdescQK, kk != 0);
       tc::umma_commit(&bars->s_full[st]);
+      tc::umma_commit(&bars->k_empty[st]);
       issued_any = true;
       return true;
     };
@@ -186,8 +207,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j + 1 < n_tiles && !issue_qk(j + 1)) break;
       if (!tc::mbar_wait(&bars->p_ready, j & 1, abort, watchdog, tc::kWatchdogAttention))
         break;
-      tc::tc_fence_after();
       const int st = j & 1;
+      if (!tc::mbar_wait(&bars->v_full[st], (j >> 1) & 1, abort, watchdog,
+                         tc::kWatchdogAttention))
+        break;
+      tc::tc_fence_after();
       const uint32_t v_addr =
           tc::smem_u32(smem + Cfg::kStageOff + st * Cfg::kStageBytes + Cfg::kTileBytes);
 #pragma unroll
@@ -198,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                      tc::smem_desc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024),
                      Cfg::kIdescPV, (j | kk) != 0);
       tc::umma_commit(&bars->pv_done);
-      tc::umma_commit(&bars->kv_empty[st]);
+      tc::umma_commit(&bars->v_empty[st]);
     }
     if (*abort && issued_any) {
       tc::umma_commit(&bars->drain);
@@ -208,11 +232,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kSoftmaxWarp0) {
     // ---------------------------------------------------------- softmax
+    // Two warpgroups share each S tile: group g owns keys [64g, 64g+64) of
+    // every row, O columns [g*D/2, (g+1)*D/2) for rescaling and output, and
+    // its own partial row sum.  Row maxima are exchanged through shared
+    // memory (double-buffered by tile parity) behind a 256-thread barrier.
+    const int g = (warp - kSoftmaxWarp0) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // row in tile == TMEM lane
     const int row = q0 + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    uint8_t* p_tile = smem + Cfg::kPOff;
+    float* xchg = reinterpret_cast<float*>(smem + Cfg::kXchgOff);  // [2][2][128]
+    uint8_t* p_tile = smem + Cfg::kPOff + g * Cfg::kBoxBytes;
+    constexpr int kHalfKeys = kKeys / 2;
+    constexpr int kHalfD = D / 2;
+    const int limit = causal ? min(seq - 1, row) : seq - 1;  // last visible key
     float m_used = -INFINITY;
     float l = 0.0f;
     bool ok = true;
@@ -224,22 +257,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc::tc_fence_after();
-      float s[kKeys];
+      float s[kHalfKeys];
 #pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) {
+      for (int c = 0; c < kHalfKeys / 32; ++c) {
         float chunk[32];
-        tc::tmem_ld32(tmem + lane_off + st * kKeys + c * 32, chunk);
+        tc::tmem_ld32(tmem + lane_off + st * kKeys + g * kHalfKeys + c * 32, chunk);
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = chunk[i];
       }
-      const int key0 = j * kKeys;
-      const int limit = causal ? min(seq - 1, row) : seq - 1;  // last visible key
+      const int key0 = j * kKeys + g * kHalfKeys;
       float mx = -INFINITY;
+      if (key0 + kHalfKeys - 1 <= limit) {  // interior: nothing masked
 #pragma unroll
-      for (int i = 0; i < kKeys; ++i) {
-        s[i] = (key0 + i <= limit) ? s[i] * scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[i]);
+        for (int i = 0; i < kHalfKeys; ++i) {
+          s[i] *= scale_log2;
+          mx = fmaxf(mx, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kHalfKeys; ++i) {
+          s[i] = (key0 + i <= limit) ? s[i] * scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[i]);
+        }
       }
+      float* xm = xchg + st * 256;
+      xm[g * 128 + r] = mx;
+      named_barrier_sync(1, 256);
+      mx = fmaxf(xm[r], xm[128 + r]);
       float alpha = 1.0f;
       if (mx > m_used + kRescaleThreshold) {
         alpha = (m_used == -INFINITY) ? 0.0f : exp2f(m_used - mx);
@@ -248,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float sum = 0.0f;
 #pragma unroll
-      for (int i = 0; i < kKeys; ++i) {
+      for (int i = 0; i < kHalfKeys; ++i) {
         s[i] = exp2f(s[i] - m_used);  // -inf -> 0
         sum += s[i];
       }
@@ -263,25 +307,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tc_fence_after();
         if (__any_sync(kFullMask, alpha != 1.0f)) {
 #pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < kHalfD / 32; ++c) {
             float o[32];
-            tc::tmem_ld32(tmem_o + lane_off + c * 32, o);
+            const uint32_t col = tmem_o + lane_off + g * kHalfD + c * 32;
+            tc::tmem_ld32(col, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tc::tmem_st32(tmem_o + lane_off + c * 32, o);
+            tc::tmem_st32(col, o);
           }
         }
       }
-      // P row r -> K-major SW128 tile: 64-key blocks of 16 KB, 128 B per row,
-      // 16-byte chunk c of a row stored at chunk (c ^ (r & 7)).
+      // P row r, keys [64g, 64g+64) -> box g of the K-major SW128 tile: 128 B
+      // per row, 16-byte chunk c stored at chunk (c ^ (r & 7)).
 #pragma unroll
-      for (int c = 0; c < kKeys / 8; ++c) {
+      for (int c = 0; c < kHalfKeys / 8; ++c) {
         __align__(16) __half2 h[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
-        const int blk = c >> 3;
-        const int chunk = (c & 7) ^ (r & 7);
-        *reinterpret_cast<uint4*>(p_tile + blk * Cfg::kBoxBytes + r * 128 + chunk * 16) =
+        for (int i = 0; i < 4; ++i)
+          h[i] = __floats2half2_rn(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
+        *reinterpret_cast<uint4*>(p_tile + r * 128 + ((c ^ (r & 7)) * 16)) =
             *reinterpret_cast<const uint4*>(h);
       }
       tc::fence_proxy_async_smem();
@@ -291,12 +335,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && tc::mbar_wait_warp(&bars->pv_done, (n_tiles - 1) & 1, abort, watchdog,
                                  tc::kWatchdogAttention)) {
       tc::tc_fence_after();
-      const float inv = 1.0f / l;
-      float* orow = out + (static_cast<size_t>(bh) * seq + row) * D;
+      float* xs = xchg + 512;
+      xs[g * 128 + r] = l;
+      named_barrier_sync(1, 256);
+      const float inv = 1.0f / (xs[r] + xs[128 + r]);
+      float* orow = out + (static_cast<size_t>(bh) * seq + row) * D + g * kHalfD;
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < kHalfD / 32; ++c) {
         float o[32];
-        tc::tmem_ld32(tmem_o + lane_off + c * 32, o);
+        tc::tmem_ld32(tmem_o + lane_off + g * kHalfD + c * 32, o);
         if (row < seq) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
