@@ -2,29 +2,32 @@
 // softmax state and FP32 output (reference src/attention.cu:222-360 and
 // :486-507 -- there a 16x16 WMMA kernel with QK^T on one warp).
 //
-// One CTA = one (batch*head, 128-query tile); causal grids start with the
-// longest (bottom) tiles.  384 threads:
-//   warp 0    TMA producer: Q once; K_j and V_j (128 keys each) into two
-//             2-slot rings with separate barriers (K_{j+1} streams in as soon
-//             as QK_{j-1} is done, independent of PV), all 128-byte swizzled boxes of 64 columns from a
-//             3-D [B*H, S, D] tensor map (rows past S read as zero);
-//   warp 1    MMA issuer (one thread):
-//               S_j = Q K_j^T   M128 N128 K=D  (both K-major)   -> TMEM S[j%2]
-//               O  += P_j V_j   M128 N=D K128  (P K-major, V N-major) -> TMEM O
-//             QK_{j+1} is issued before PV_j, so the next scores are computed
-//             while the softmax warps work on tile j;
-//   warps 4-11 softmax, two warpgroups, each owning half the keys of every
-//             row (thread = query row = TMEM lane; 64 fp32 scores in
-//             registers): mask only on edge tiles (keys >= S, causal), row
-//             max exchanged between the groups in shared memory, running max
-//             in the log2 domain, P = exp2(s - m) rounded to FP16 into a
-//             swizzled shared tile (the A operand of PV), row sum in FP32
-//             (per group, added at the end).  The running max
-//             used for P is only moved when a row's maximum grows by more
-//             than 8 (a factor 256), so O in TMEM is rescaled rarely; P then
-//             stays <= 256, well inside FP16.  At the end O / l is stored.
-//   warps 2-3 idle after set-up.
-// TMEM: S double buffer (2 x 128 columns) + O (D columns) within 512.
+// One CTA = one (batch*head, pair of 128-query tiles A and B) -- or a single
+// tile A when pairs would leave SMs idle; causal grids start with the
+// longest (bottom) pairs.  320 threads:
+//   warp 0     TMA producer: Q_A, Q_B once; K_j and V_j (128 keys each)
+//              into two 2-slot rings with separate barriers, all 128-byte
+//              swizzled 64-column boxes of a 3-D [B*H, S, D] tensor map
+//              (rows past S read as zero);
+//   warp 1     MMA issuer (one thread), ping-pong over the two tiles:
+//                PV_A(j), QK_A(j+1), PV_B(j), QK_B(j+1), ...
+//              S_X = Q_X K^T: M128 N128 K=D, both operands K-major in smem;
+//              O_X += P_X V:  M128 N=D K128, P_X read from TMEM, V N-major in
+//              smem -- so while one tile's softmax runs, the tensor pipe
+//              works on the other tile;
+//   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B (thread = query
+//              row = TMEM lane, 128 fp32 scores in registers): mask only on
+//              edge tiles, running max in the log2 domain, P = 2^(s - m) with
+//              3 of every 4 exponentials on the MUFU unit and 1 as a
+//              polynomial on the FMA pipe, P packed to FP16 and stored back
+//              into the first 64 columns of the tile's own S columns (the
+//              TMEM A operand of PV), row sum in FP32.  The max used for P
+//              only moves when a row's maximum grows by more than 8 (a factor
+//              256), so O is rarely rescaled and P stays <= 256 (FP16-safe).
+// TMEM: S_A, S_B (128 columns each), O_A, O_B (D columns each).
+// Ordering: tcgen05.mma ops of one thread run in issue order, and the commit
+// that signals S_X(j) follows PV_X(j-1); so when a softmax warp sees S_X(j),
+// the previous P_X was consumed and O_X is stable for rescaling.
 //
 // All waits are bounded (tc_common.cuh); on giving up the CTA drains its
 // TMA loads and MMAs, frees TMEM and exits, recording the watchdog word.
@@ -38,26 +41,24 @@ namespace {
 
 constexpr int kRowsQ = 128;
 constexpr int kKeys = 128;
-constexpr int kThreads = 384;
-constexpr int kSoftmaxWarp0 = 4;
+constexpr int kThreads = 320;
+constexpr int kSoftmaxWarp0 = 2;  // warps 2-5: tile A, warps 6-9: tile B
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 template <int D>
 struct AttnCfg {
-  static constexpr int kBoxes = D / 64;                    // 64-column boxes per row
-  static constexpr int kTileBytes = kRowsQ * D * 2;        // Q, K or V tile
-  static constexpr int kBoxBytes = kRowsQ * 64 * 2;        // 16 KB
-  static constexpr int kPBytes = kRowsQ * kKeys * 2;       // 32 KB
-  static constexpr int kStageBytes = 2 * kTileBytes;       // K + V
-  static constexpr int kQOff = 0;
-  static constexpr int kStageOff = kTileBytes;
-  static constexpr int kPOff = kStageOff + 2 * kStageBytes;
-  static constexpr int kXchgOff = kPOff + kPBytes;             // 3 x 256 floats
-  static constexpr int kBarOff = kXchgOff + 3 * 256 * 4;
+  static constexpr int kBoxes = D / 64;              // 64-column boxes per row
+  static constexpr int kTileBytes = kRowsQ * D * 2;  // one Q, K or V tile
+  static constexpr int kBoxBytes = kRowsQ * 64 * 2;  // 16 KB
+  static constexpr int kQOff = 0;                    // Q_A, Q_B
+  static constexpr int kKOff = 2 * kTileBytes;       // K slots 0, 1
+  static constexpr int kVOff = 4 * kTileBytes;       // V slots 0, 1
+  static constexpr int kBarOff = 6 * kTileBytes;
   static constexpr size_t kSmem = kBarOff + 256 + 1024;
   static constexpr uint32_t kIdescQK = tc::idesc_f16_f32(kRowsQ, kKeys, false, false);
   static constexpr uint32_t kIdescPV = tc::idesc_f16_f32(kRowsQ, D, false, true);
+  static constexpr uint32_t kColO0 = 2 * kKeys;  // O_A; O_B follows at +D
 };
 
 struct AttnBars {
@@ -66,17 +67,14 @@ struct AttnBars {
   uint64_t k_empty[2];
   uint64_t v_full[2];
   uint64_t v_empty[2];
-  uint64_t s_full[2];
-  uint64_t p_ready;
-  uint64_t pv_done;
+  uint64_t s_full[2];   // per tile X
+  uint64_t p_ready[2];  // per tile X
+  uint64_t o_done;
+  uint64_t pv_done;  // single-tile mode: PV(j) complete
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
 };
-
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
 
 // K-major SW128 operand made of 64-column boxes of 128 rows: the 16-wide K
 // step kk lives in box kk/4 at byte offset 32*(kk%4).
@@ -84,13 +82,42 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, int box_b
   return tc::smem_desc_sw128(base + (kk >> 2) * box_bytes + (kk & 3) * 32, 16, 1024);
 }
 
+// 2^x on the FMA/ALU pipes (x <= 8 here; very negative x gives ~0).
+// Range reduction x = n + f, n = round-to-nearest(x), |f| <= 1/2, by adding
+// 1.5 * 2^23 (the rounded integer lands in the low mantissa bits); 2^f from a
+// cubic fitted by least squares on relative error over [-1/2, 1/2] (max
+// relative error 7.6e-5, below FP16's 4.9e-4 half-ulp: the value is rounded
+// to FP16 for the PV product; tests/test_exp2_poly.py re-derives the fit);
+// then n is added to the exponent field.
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float shifter = 12582912.0f;  // 1.5 * 2^23
+  const float t = x + shifter;
+  const float n = t - shifter;
+  const float f = x - n;
+  float p = fmaf(0.05513019859790802f, f, 0.24260807037353516f);
+  p = fmaf(p, f, 0.6932686567306519f);
+  p = fmaf(p, f, 0.9999284744262695f);
+  const int ni = __float_as_int(t) - 0x4B400000;
+  return __int_as_float(__float_as_int(p) + (ni << 23));
+}
+
+__device__ __forceinline__ float pack_half2_bits(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return __uint_as_float(*reinterpret_cast<const uint32_t*>(&h));
+}
+
+}  // namespace
+
+namespace {
+
 template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v, float* __restrict__ out,
                         int heads_total, int seq, int causal, float scale_log2,
-                        int* watchdog) {
+                        int tiles_per_cta, int* watchdog) {
   using Cfg = AttnCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -101,11 +128,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   const int q_tiles = (seq + kRowsQ - 1) / kRowsQ;
+  const int pairs = (q_tiles + tiles_per_cta - 1) / tiles_per_cta;
   const int bh = blockIdx.x % heads_total;
-  const int qb = q_tiles - 1 - static_cast<int>(blockIdx.x / heads_total);
-  const int q0 = qb * kRowsQ;
-  const int kv_tiles_all = (seq + kKeys - 1) / kKeys;
-  const int n_tiles = causal ? min(kv_tiles_all, (q0 + kRowsQ - 1) / kKeys + 1) : kv_tiles_all;
+  const int pair = pairs - 1 - static_cast<int>(blockIdx.x / heads_total);
+  const int qt0 = tiles_per_cta * pair;
+  const bool valid_b = tiles_per_cta == 2 && qt0 + 1 < q_tiles;
+  const int kv_all = (seq + kKeys - 1) / kKeys;
+  int n_tiles[2];
+  n_tiles[0] = causal ? min(kv_all, qt0 + 1) : kv_all;
+  n_tiles[1] = valid_b ? (causal ? min(kv_all, qt0 + 2) : kv_all) : 0;
+  const int n_max = max(n_tiles[0], n_tiles[1]);
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->q_full, 1);
@@ -115,8 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&bars->v_full[i], 1);
       tc::mbar_init(&bars->v_empty[i], 1);
       tc::mbar_init(&bars->s_full[i], 1);
+      tc::mbar_init(&bars->p_ready[i], 128);
     }
-    tc::mbar_init(&bars->p_ready, 256);
+    tc::mbar_init(&bars->o_done, 1);
     tc::mbar_init(&bars->pv_done, 1);
     tc::mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -130,30 +163,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
-  const uint32_t tmem_o = tmem + 2 * kKeys;
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------- producer
-    // K and V have separate slots and barriers: K_{j+1} only waits for
-    // QK_{j-1} to finish with its slot, V_{j+1} for PV_{j-1}.
     uint32_t issued_mask = 0, issued_parity = 0;  // bit s: K slot s, bit 2+s: V slot s
-    tc::mbar_expect_tx(&bars->q_full, Cfg::kTileBytes);
+    tc::mbar_expect_tx(&bars->q_full, (valid_b ? 2 : 1) * Cfg::kTileBytes);
+    for (int x = 0; x < (valid_b ? 2 : 1); ++x)
 #pragma unroll
-    for (int b = 0; b < Cfg::kBoxes; ++b)
-      tc::tma_load_3d(smem + Cfg::kQOff + b * Cfg::kBoxBytes, &map_q, b * 64, q0, bh,
-                      &bars->q_full);
-    for (int j = 0; j < n_tiles && !*abort; ++j) {
+      for (int b = 0; b < Cfg::kBoxes; ++b)
+        tc::tma_load_3d(smem + Cfg::kQOff + x * Cfg::kTileBytes + b * Cfg::kBoxBytes, &map_q,
+                        b * 64, (qt0 + x) * kRowsQ, bh, &bars->q_full);
+    for (int j = 0; j < n_max && !*abort; ++j) {
       const int st = j & 1;
       const uint32_t ph = (j >> 1) & 1;
-      uint8_t* ks = smem + Cfg::kStageOff + st * Cfg::kStageBytes;
-      uint8_t* vs = ks + Cfg::kTileBytes;
       if (!tc::mbar_wait(&bars->k_empty[st], ph ^ 1, abort, watchdog, tc::kWatchdogAttention))
         break;
       tc::mbar_expect_tx(&bars->k_full[st], Cfg::kTileBytes);
 #pragma unroll
       for (int b = 0; b < Cfg::kBoxes; ++b)
-        tc::tma_load_3d(ks + b * Cfg::kBoxBytes, &map_k, b * 64, j * kKeys, bh,
-                        &bars->k_full[st]);
+        tc::tma_load_3d(smem + Cfg::kKOff + st * Cfg::kTileBytes + b * Cfg::kBoxBytes, &map_k,
+                        b * 64, j * kKeys, bh, &bars->k_full[st]);
       issued_mask |= 1u << st;
       issued_parity = (issued_parity & ~(1u << st)) | (ph << st);
       if (!tc::mbar_wait(&bars->v_empty[st], ph ^ 1, abort, watchdog, tc::kWatchdogAttention))
@@ -161,12 +190,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_expect_tx(&bars->v_full[st], Cfg::kTileBytes);
 #pragma unroll
       for (int b = 0; b < Cfg::kBoxes; ++b)
-        tc::tma_load_3d(vs + b * Cfg::kBoxBytes, &map_v, b * 64, j * kKeys, bh,
-                        &bars->v_full[st]);
+        tc::tma_load_3d(smem + Cfg::kVOff + st * Cfg::kTileBytes + b * Cfg::kBoxBytes, &map_v,
+                        b * 64, j * kKeys, bh, &bars->v_full[st]);
       issued_mask |= 4u << st;
       issued_parity = (issued_parity & ~(4u << st)) | (ph << (st + 2));
     }
-    if (*abort) {
+    if (*abort) {  // let in-flight TMA writes land before the CTA exits
       const uint32_t qa = tc::smem_u32(&bars->q_full);
       for (uint32_t i = 0; i < tc::kMaxPolls && !tc::mbar_try_wait(qa, 0); ++i) {
       }
@@ -181,50 +210,88 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------- MMA issuer
     bool issued_any = false;
     const uint32_t q_addr = tc::smem_u32(smem + Cfg::kQOff);
-    const uint32_t p_addr = tc::smem_u32(smem + Cfg::kPOff);
-    auto issue_qk = [&](int j) -> bool {
-      const int st = j & 1;
-      if (!tc::mbar_wait(&bars->k_full[st], (j >> 1) & 1, abort, watchdog,
-                         tc::kWatchdogAttention))
-        return false;
-      tc::tc_fence_after();
-      const uint32_t k_addr = tc::smem_u32(smem + Cfg::kStageOff + st * Cfg::kStageBytes);
+    // S block `buf` = Q_x K_j^T (K_j already landed); commit signals s_full[buf].
+    auto qk_into = [&](int buf, int x, int j) {
+      const uint32_t k_addr = tc::smem_u32(smem + Cfg::kKOff + (j & 1) * Cfg::kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk)
-        tc::umma_f16(tmem + st * kKeys, kmajor_desc(q_addr, kk, Cfg::kBoxBytes),
+        tc::umma_f16(tmem + buf * kKeys,
+                     kmajor_desc(q_addr + x * Cfg::kTileBytes, kk, Cfg::kBoxBytes),
                      kmajor_desc(k_addr, kk, Cfg::kBoxBytes), Cfg::kIdescQK, kk != 0);
-      tc::umma_commit(&bars->s_full[st]);
-      tc::umma_commit(&bars->k_empty[st]);
+      tc::umma_commit(&bars->s_full[buf]);
       issued_any = true;
-      return true;
     };
-    bool ok = tc::mbar_wait(&bars->q_full, 0, abort, watchdog, tc::kWatchdogAttention);
-    if (ok) {
-      tc::tc_fence_after();
-      ok = issue_qk(0);
-    }
-    for (int j = 0; ok && j < n_tiles; ++j) {
-      if (j + 1 < n_tiles && !issue_qk(j + 1)) break;
-      if (!tc::mbar_wait(&bars->p_ready, j & 1, abort, watchdog, tc::kWatchdogAttention))
-        break;
-      const int st = j & 1;
-      if (!tc::mbar_wait(&bars->v_full[st], (j >> 1) & 1, abort, watchdog,
-                         tc::kWatchdogAttention))
-        break;
-      tc::tc_fence_after();
-      const uint32_t v_addr =
-          tc::smem_u32(smem + Cfg::kStageOff + st * Cfg::kStageBytes + Cfg::kTileBytes);
+    auto qk = [&](int x, int j) { qk_into(x, x, j); };
+    // O_x += P (FP16 pairs in the first 64 columns of S block `buf`; 8
+    // packed columns per 16 keys) * V_j.
+    auto pv_from = [&](int buf, int x, int j) {
+      const uint32_t v_addr = tc::smem_u32(smem + Cfg::kVOff + (j & 1) * Cfg::kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk)
         // V: N-major (D contiguous), 64-column boxes of 128 keys (16 KB
         // apart); a 16-key step is two 8-row groups (2 KB).
-        tc::umma_f16(tmem_o, kmajor_desc(p_addr, kk, Cfg::kBoxBytes),
-                     tc::smem_desc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024),
-                     Cfg::kIdescPV, (j | kk) != 0);
-      tc::umma_commit(&bars->pv_done);
-      tc::umma_commit(&bars->v_empty[st]);
+        tc::umma_f16_tmem_a(tmem + Cfg::kColO0 + x * D, tmem + buf * kKeys + kk * 8,
+                            tc::smem_desc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024),
+                            Cfg::kIdescPV, (j | kk) != 0);
+      issued_any = true;
+    };
+    auto pv = [&](int x, int j) { pv_from(x, x, j); };
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      const bool ok = tc::mbar_wait(bar, parity, abort, watchdog, tc::kWatchdogAttention);
+      if (ok) tc::tc_fence_after();
+      return ok;
+    };
+    bool ok = wait(&bars->q_full, 0) && wait(&bars->k_full[0], 0);
+    if (tiles_per_cta == 1) {
+      // One tile: S alternates between the two S column blocks, so QK(j+1)
+      // runs while the softmax works on S(j).
+      if (ok) {
+        qk(0, 0);  // into block 0
+        tc::umma_commit(&bars->k_empty[0]);
+      }
+      const int n = n_tiles[0];
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) {
+          if (!wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) break;
+          qk_into((j + 1) & 1, 0, j + 1);
+          tc::umma_commit(&bars->k_empty[(j + 1) & 1]);
+        }
+        if (!wait(&bars->v_full[j & 1], (j >> 1) & 1)) break;
+        if (!wait(&bars->p_ready[0], j & 1)) break;
+        pv_from(j & 1, 0, j);
+        tc::umma_commit(&bars->pv_done);
+        tc::umma_commit(&bars->v_empty[j & 1]);
+      }
+    } else {
+      if (ok) {
+        qk(0, 0);
+        if (n_tiles[1] > 0) qk(1, 0);
+        tc::umma_commit(&bars->k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_max; ++j) {
+        const bool do_a = j < n_tiles[0], do_b = j < n_tiles[1];
+        const bool next_a = j + 1 < n_tiles[0], next_b = j + 1 < n_tiles[1];
+        if (!wait(&bars->v_full[j & 1], (j >> 1) & 1)) break;
+        if (do_a) {
+          if (!wait(&bars->p_ready[0], j & 1)) break;
+          pv(0, j);
+        }
+        if (next_a || next_b) {
+          if (!wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) break;
+        }
+        if (next_a) qk(0, j + 1);
+        if (do_b) {
+          if (!wait(&bars->p_ready[1], j & 1)) break;
+          pv(1, j);
+        }
+        tc::umma_commit(&bars->v_empty[j & 1]);
+        if (next_b) qk(1, j + 1);
+        if (next_a || next_b) tc::umma_commit(&bars->k_empty[(j + 1) & 1]);
+      }
     }
-    if (*abort && issued_any) {
+    if (!*abort) {
+      tc::umma_commit(&bars->o_done);
+    } else if (issued_any) {  // wait for issued MMAs before TMEM is freed
       tc::umma_commit(&bars->drain);
       const uint32_t a = tc::smem_u32(&bars->drain);
       for (uint32_t i = 0; i < tc::kMaxPolls && !tc::mbar_try_wait(a, 0); ++i) {
@@ -232,118 +299,101 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kSoftmaxWarp0) {
     // ---------------------------------------------------------- softmax
-    // Two warpgroups share each S tile: group g owns keys [64g, 64g+64) of
-    // every row, O columns [g*D/2, (g+1)*D/2) for rescaling and output, and
-    // its own partial row sum.  Row maxima are exchanged through shared
-    // memory (double-buffered by tile parity) behind a 256-thread barrier.
-    const int g = (warp - kSoftmaxWarp0) >> 2;
+    const int x = (warp - kSoftmaxWarp0) >> 2;  // tile A or B
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // row in tile == TMEM lane
-    const int row = q0 + r;
+    const int row = (qt0 + x) * kRowsQ + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    float* xchg = reinterpret_cast<float*>(smem + Cfg::kXchgOff);  // [2][2][128]
-    uint8_t* p_tile = smem + Cfg::kPOff + g * Cfg::kBoxBytes;
-    constexpr int kHalfKeys = kKeys / 2;
-    constexpr int kHalfD = D / 2;
+    const bool single = tiles_per_cta == 1;
+    const uint32_t o_col = tmem + lane_off + Cfg::kColO0 + x * D;
     const int limit = causal ? min(seq - 1, row) : seq - 1;  // last visible key
+    const int n = n_tiles[x];
     float m_used = -INFINITY;
     float l = 0.0f;
-    bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
-      if (!tc::mbar_wait_warp(&bars->s_full[st], (j >> 1) & 1, abort, watchdog,
-                              tc::kWatchdogAttention)) {
+    bool ok = n > 0;
+    for (int j = 0; ok && j < n; ++j) {
+      // S block: the tile's own in pair mode, alternating in single mode.
+      const int buf = single ? (j & 1) : x;
+      const uint32_t s_col = tmem + lane_off + buf * kKeys;
+      if (!tc::mbar_wait_warp(&bars->s_full[buf], single ? (j >> 1) & 1 : j & 1, abort,
+                              watchdog, tc::kWatchdogAttention)) {
         ok = false;
         break;
       }
       tc::tc_fence_after();
-      float s[kHalfKeys];
+      float s[kKeys];
 #pragma unroll
-      for (int c = 0; c < kHalfKeys / 32; ++c) {
+      for (int c = 0; c < kKeys / 32; ++c) {
         float chunk[32];
-        tc::tmem_ld32(tmem + lane_off + st * kKeys + g * kHalfKeys + c * 32, chunk);
+        tc::tmem_ld32(s_col + c * 32, chunk);
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = chunk[i];
       }
-      const int key0 = j * kKeys + g * kHalfKeys;
-      float mx = -INFINITY;
-      if (key0 + kHalfKeys - 1 <= limit) {  // interior: nothing masked
+      const int key0 = j * kKeys;
+      if (key0 + kKeys - 1 > limit) {  // edge tile: mask keys past the limit
 #pragma unroll
-        for (int i = 0; i < kHalfKeys; ++i) {
-          s[i] *= scale_log2;
-          mx = fmaxf(mx, s[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kHalfKeys; ++i) {
-          s[i] = (key0 + i <= limit) ? s[i] * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[i]);
-        }
+        for (int i = 0; i < kKeys; ++i)
+          if (key0 + i > limit) s[i] = -INFINITY;
       }
-      float* xm = xchg + st * 256;
-      xm[g * 128 + r] = mx;
-      named_barrier_sync(1, 256);
-      mx = fmaxf(xm[r], xm[128 + r]);
+      // Raw-score maximum (scale > 0 commutes with max); eight independent
+      // partial maxima / sums keep dependency chains short.
+      float pm[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) pm[a] = s[a];
+#pragma unroll
+      for (int i = 8; i < kKeys; ++i) pm[i & 7] = fmaxf(pm[i & 7], s[i]);
+      const float mx = scale_log2 * fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                                          fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       float alpha = 1.0f;
       if (mx > m_used + kRescaleThreshold) {
         alpha = (m_used == -INFINITY) ? 0.0f : exp2f(m_used - mx);
         m_used = mx;
         l *= alpha;
       }
-      float sum = 0.0f;
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kHalfKeys; ++i) {
-        s[i] = exp2f(s[i] - m_used);  // -inf -> 0
-        sum += s[i];
+      for (int i = 0; i < kKeys; ++i) {
+        const float arg = fmaf(s[i], scale_log2, -m_used);  // -inf -> 0 below
+        s[i] = (i & 3) == 3 ? exp2_poly(arg) : exp2f(arg);
+        ps[i & 7] += s[i];
       }
-      l += sum;
-      // P_{j-1} must be consumed (PV_{j-1} done) before P and O are touched.
-      if (j > 0) {
-        if (!tc::mbar_wait_warp(&bars->pv_done, (j - 1) & 1, abort, watchdog,
-                                tc::kWatchdogAttention)) {
+      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      // P as packed FP16 pairs (packed in place, front to back) into the
+      // first 64 columns of S_x.
+#pragma unroll
+      for (int i = 0; i < kKeys / 2; ++i) s[i] = pack_half2_bits(s[2 * i], s[2 * i + 1]);
+      tc::tmem_st32(s_col, s);
+      tc::tmem_st32(s_col + 32, s + 32);
+      // O_x is stable here (S_x(j) was committed after PV_x(j-1), and
+      // PV_x(j) waits for p_ready); rescaled after P is out of registers.
+      if (j > 0 && __any_sync(kFullMask, alpha != 1.0f)) {
+        // Single mode: S(j) was issued before PV(j-1), so wait for it here.
+        if (single && !tc::mbar_wait_warp(&bars->pv_done, (j - 1) & 1, abort, watchdog,
+                                          tc::kWatchdogAttention)) {
           ok = false;
           break;
         }
         tc::tc_fence_after();
-        if (__any_sync(kFullMask, alpha != 1.0f)) {
 #pragma unroll 1
-          for (int c = 0; c < kHalfD / 32; ++c) {
-            float o[32];
-            const uint32_t col = tmem_o + lane_off + g * kHalfD + c * 32;
-            tc::tmem_ld32(col, o);
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tc::tmem_ld32(o_col + c * 32, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tc::tmem_st32(col, o);
-          }
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tc::tmem_st32(o_col + c * 32, o);
         }
       }
-      // P row r, keys [64g, 64g+64) -> box g of the K-major SW128 tile: 128 B
-      // per row, 16-byte chunk c stored at chunk (c ^ (r & 7)).
-#pragma unroll
-      for (int c = 0; c < kHalfKeys / 8; ++c) {
-        __align__(16) __half2 h[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          h[i] = __floats2half2_rn(s[c * 8 + 2 * i], s[c * 8 + 2 * i + 1]);
-        *reinterpret_cast<uint4*>(p_tile + r * 128 + ((c ^ (r & 7)) * 16)) =
-            *reinterpret_cast<const uint4*>(h);
-      }
-      tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&bars->p_ready);
+      tc::mbar_arrive(&bars->p_ready[x]);
     }
-    if (ok && tc::mbar_wait_warp(&bars->pv_done, (n_tiles - 1) & 1, abort, watchdog,
-                                 tc::kWatchdogAttention)) {
+    if (ok && tc::mbar_wait_warp(&bars->o_done, 0, abort, watchdog, tc::kWatchdogAttention)) {
       tc::tc_fence_after();
-      float* xs = xchg + 512;
-      xs[g * 128 + r] = l;
-      named_barrier_sync(1, 256);
-      const float inv = 1.0f / (xs[r] + xs[128 + r]);
-      float* orow = out + (static_cast<size_t>(bh) * seq + row) * D + g * kHalfD;
+      const float inv = 1.0f / l;
+      float* orow = out + (static_cast<size_t>(bh) * seq + row) * D;
 #pragma unroll 1
-      for (int c = 0; c < kHalfD / 32; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         float o[32];
-        tc::tmem_ld32(tmem_o + lane_off + g * kHalfD + c * 32, o);
+        tc::tmem_ld32(o_col + c * 32, o);
         if (row < seq) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
@@ -381,12 +431,18 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(Cfg::kSmem));
   if (e != cudaSuccess) return e;
-  const long long ctas = static_cast<long long>(heads_total) * ((seq + kRowsQ - 1) / kRowsQ);
+  // Two query tiles per CTA (tensor-pipe ping-pong) unless that would leave
+  // SMs idle; then one tile per CTA for twice the CTAs.
+  const long long q_tiles = (seq + kRowsQ - 1) / kRowsQ;
+  const int tiles_per_cta =
+      (static_cast<long long>(heads_total) * ((q_tiles + 1) / 2) >= 2LL * sm_count()) ? 2 : 1;
+  const long long ctas =
+      static_cast<long long>(heads_total) * ((q_tiles + tiles_per_cta - 1) / tiles_per_cta);
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   attention_tc_kernel<D><<<static_cast<unsigned>(ctas), kThreads, Cfg::kSmem, stream>>>(
       maps[0], maps[1], maps[2], out, heads_total, seq, causal ? 1 : 0, scale_log2,
-      watchdog_word());
+      tiles_per_cta, watchdog_word());
   return cudaGetLastError();
 }
 

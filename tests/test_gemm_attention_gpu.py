@@ -135,3 +135,19 @@ def test_attention_f32_baseline_shape_sampled_heads(cuda, stream):
         got = run_attention(cuda, stream, q, k, v, causal)
         want = orc.attention(q[:, :2], k[:, :2], v[:, :2], causal)
         np.testing.assert_allclose(got[:, :2], want, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("b,h,s,d,causal", [
+    (4, 40, 640, 128, True),    # 160 heads x 3 tile pairs, last pair single
+    (8, 20, 512, 64, False),    # D = 64
+    (2, 80, 768, 128, False),
+])
+def test_attention_f16_paired_tiles_sampled_heads(cuda, stream, b, h, s, d, causal):
+    """Grids big enough for the two-query-tiles-per-CTA schedule; the oracle
+    checks a spread of heads."""
+    q, k, v = att_inputs((b, h, s, d), None, b * h + s + d, np.float16)
+    got = run_attention(cuda, stream, q, k, v, causal).reshape(b * h, s, d)
+    idx = np.unique(np.linspace(0, b * h - 1, 5).astype(int))
+    qf, kf, vf = (x.reshape(b * h, s, d)[idx][None].astype(np.float32) for x in (q, k, v))
+    want = orc.attention(qf, kf, vf, causal)[0]
+    check_f16(got[idx], want)
