@@ -55,6 +55,75 @@ __global__ void __launch_bounds__(kBlock)
   store_row<kGroup, kItems, kVec>(output + offset, hidden, t, v);
 }
 
+// Rows of 2049..4096 floats (16-byte aligned): one 128-thread CTA per row;
+// each thread keeps 4 of its 8 float4 in registers and streams the other 4
+// into shared memory with cp.async (16-byte copies that hold no registers
+// while in flight).  At <= 32 registers and 8 KB of shared memory, 16 CTAs
+// fit per SM, so every row of 2048 x 4096 is in flight at once; caching the
+// whole row in registers (64 per thread) allows only 8 CTAs per SM and the
+// grid runs in 1.73 waves.
+constexpr int kRmsSplitThreads = 128;
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kRmsSplitThreads, 16)
+    rmsnorm_split_kernel(const float* __restrict__ input, const float* __restrict__ weight,
+                         float* __restrict__ output, int hidden, float epsilon) {
+  __shared__ __align__(16) float4 half_row[4 * kRmsSplitThreads];
+  __shared__ float scratch[kRmsSplitThreads / 32];
+  const int t = threadIdx.x;
+  const int vectors = hidden >> 2;  // 513 .. 1024
+  const float4* x4 = reinterpret_cast<const float4*>(input + static_cast<size_t>(blockIdx.x) * hidden);
+  // Slots t + 128*j: j = 0..3 in registers, j = 4..7 through shared memory.
+#pragma unroll
+  for (int j = 4; j < 8; ++j) {
+    const int idx = t + j * kRmsSplitThreads;
+    if (idx < vectors) cp_async16(&half_row[t + (j - 4) * kRmsSplitThreads], x4 + idx);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  float4 v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = ld_stream(x4 + t + j * kRmsSplitThreads);  // 4*128 < 513
+  float sq = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    sq = fmaf(v[j].x, v[j].x, sq);
+    sq = fmaf(v[j].y, v[j].y, sq);
+    sq = fmaf(v[j].z, v[j].z, sq);
+    sq = fmaf(v[j].w, v[j].w, sq);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");  // each thread reads only its own copies
+#pragma unroll
+  for (int j = 4; j < 8; ++j) {
+    if (t + j * kRmsSplitThreads < vectors) {
+      const float4 u = half_row[t + (j - 4) * kRmsSplitThreads];
+      sq = fmaf(u.x, u.x, sq);
+      sq = fmaf(u.y, u.y, sq);
+      sq = fmaf(u.z, u.z, sq);
+      sq = fmaf(u.w, u.w, sq);
+    }
+  }
+  sq = group_reduce<kRmsSplitThreads, kRmsSplitThreads, false>(sq, scratch);
+  const float inverse_rms = rsqrtf(sq / static_cast<float>(hidden) + epsilon);
+  const float4* w4 = reinterpret_cast<const float4*>(weight);
+  float4* y4 = reinterpret_cast<float4*>(output + static_cast<size_t>(blockIdx.x) * hidden);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int idx = t + j * kRmsSplitThreads;
+    if (idx < vectors) {
+      const float4 u = j < 4 ? v[j] : half_row[t + (j - 4) * kRmsSplitThreads];
+      const float4 w = __ldg(w4 + idx);
+      st_stream(y4 + idx, make_float4(u.x * inverse_rms * w.x, u.y * inverse_rms * w.y,
+                                      u.z * inverse_rms * w.z, u.w * inverse_rms * w.w));
+    }
+  }
+}
+
 constexpr int kRmsLongThreads = 1024;
 
 __global__ void __launch_bounds__(kRmsLongThreads)
@@ -86,6 +155,11 @@ extern "C" int opl_rmsnorm_f32(const float* input, const float* weight,
     return cudaErrorInvalidValue;
   const bool vec = (hidden % 4 == 0) && aligned16(input) && aligned16(output) &&
                    aligned16(weight);
+  if (vec && hidden > 2048 && hidden <= 4096) {
+    rmsnorm_split_kernel<<<tokens, kRmsSplitThreads, 0, stream>>>(input, weight, output,
+                                                                  hidden, epsilon);
+    return cudaGetLastError();
+  }
   RowShape shape;
   if (!pick_row_shape(vec ? hidden / 4 : hidden, vec, &shape)) {
     rmsnorm_long_kernel<<<tokens, kRmsLongThreads, 0, stream>>>(
