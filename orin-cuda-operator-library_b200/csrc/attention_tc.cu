@@ -17,9 +17,8 @@
 //              works on the other tile;
 //   warps 2-5  softmax of tile A, warps 6-9 softmax of tile B (thread = query
 //              row = TMEM lane, 128 fp32 scores in registers): mask only on
-//              edge tiles, running max in the log2 domain, P = 2^(s - m) with
-//              3 of every 4 exponentials on the MUFU unit and 1 as a
-//              polynomial on the FMA pipe, P packed to FP16 and stored back
+//              edge tiles, running max in the log2 domain, P = 2^(s - m) on
+//              the MUFU unit, P packed to FP16 and stored back
 //              into the first 64 columns of the tile's own S columns (the
 //              TMEM A operand of PV), row sum in FP32.  The max used for P
 //              only moves when a row's maximum grows by more than 8 (a factor
@@ -82,24 +81,12 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, int box_b
   return tc::smem_desc_sw128(base + (kk >> 2) * box_bytes + (kk & 3) * 32, 16, 1024);
 }
 
-// 2^x on the FMA/ALU pipes (x <= 8 here; very negative x gives ~0).
-// Range reduction x = n + f, n = round-to-nearest(x), |f| <= 1/2, by adding
-// 1.5 * 2^23 (the rounded integer lands in the low mantissa bits); 2^f from a
-// cubic fitted by least squares on relative error over [-1/2, 1/2] (max
-// relative error 7.6e-5, below FP16's 4.9e-4 half-ulp: the value is rounded
-// to FP16 for the PV product; tests/test_exp2_poly.py re-derives the fit);
-// then n is added to the exponent field.
-__device__ __forceinline__ float exp2_poly(float x) {
-  x = fmaxf(x, -126.0f);
-  const float shifter = 12582912.0f;  // 1.5 * 2^23
-  const float t = x + shifter;
-  const float n = t - shifter;
-  const float f = x - n;
-  float p = fmaf(0.05513019859790802f, f, 0.24260807037353516f);
-  p = fmaf(p, f, 0.6932686567306519f);
-  p = fmaf(p, f, 0.9999284744262695f);
-  const int ni = __float_as_int(t) - 0x4B400000;
-  return __int_as_float(__float_as_int(p) + (ni << 23));
+// 2^x by the MUFU ex2 instruction (flushes subnormal results to zero;
+// 2^-inf = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ float pack_half2_bits(float lo, float hi) {
@@ -322,12 +309,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc::tc_fence_after();
       float s[kKeys];
+      {
+        uint32_t raw[kKeys];
 #pragma unroll
-      for (int c = 0; c < kKeys / 32; ++c) {
-        float chunk[32];
-        tc::tmem_ld32(s_col + c * 32, chunk);
+        for (int c = 0; c < kKeys / 32; ++c) tc::tmem_ld32_nowait(s_col + c * 32, raw + c * 32);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = chunk[i];
+        for (int c = 0; c < kKeys / 32; ++c) tc::tmem_wait_ld32(raw + c * 32);
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) s[i] = __uint_as_float(raw[i]);
       }
       const int key0 = j * kKeys;
       if (key0 + kKeys - 1 > limit) {  // edge tile: mask keys past the limit
@@ -350,11 +339,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = mx;
         l *= alpha;
       }
+      // 2^(s*scale - m) for all 128 keys on the MUFU unit (ex2.approx,
+      // relative error ~2^-22, far below the FP16 rounding of P), eight
+      // independent partial sums.  Measured on B200, MUFU throughput is the
+      // softmax's limit; an FMA-pipe polynomial for part of the keys cost
+      // more issue slots than it saved.
       float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < kKeys; ++i) {
-        const float arg = fmaf(s[i], scale_log2, -m_used);  // -inf -> 0 below
-        s[i] = (i & 3) == 3 ? exp2_poly(arg) : exp2f(arg);
+        s[i] = fast_exp2(fmaf(s[i], scale_log2, -m_used));  // -inf -> 0
         ps[i & 7] += s[i];
       }
       l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
