@@ -10,8 +10,9 @@
 //           M=128 N=256 K=16 per K block into a TMEM accumulator; commits
 //           release the smem stage ("empty") and, after the last K block,
 //           hand the accumulator to the epilogue ("tmem_full");
-//   warps 2-5 epilogue: tcgen05.ld of their 32 TMEM lanes (one C row per
-//           thread), predicated FP32 stores, then "tmem_empty".
+//   warps 2-5 epilogue: tcgen05.ld of their 32 TMEM lanes, a per-warp
+//           transpose through shared memory, coalesced predicated FP32
+//           row stores, then "tmem_empty".
 // The 512 TMEM columns hold two 128x256 FP32 accumulators, so the epilogue of
 // tile i overlaps the main loop of tile i+1.  Tiles are walked in groups of
 // 16 M blocks so concurrently running CTAs share A and B panels in L2.
@@ -41,7 +42,9 @@ constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kGroupM = 16;
 constexpr uint32_t kIdesc = tc::idesc_f16_f32(kBM, kBN, false, true);
-constexpr size_t kSmemBytes = kStages * kStageBytes + 1024 + 256;
+constexpr int kStagePitch = 33;                          // floats per staged row
+constexpr int kEpiStageBytes = 4 * 32 * kStagePitch * 4;  // 4 warps x 32x33 floats
+constexpr size_t kSmemBytes = kStages * kStageBytes + kEpiStageBytes + 1024 + 256;
 
 struct Barriers {
   uint64_t full[kStages];
@@ -73,7 +76,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes);
+  float* epi_stage = reinterpret_cast<float*>(smem + kStages * kStageBytes);
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + kStages * kStageBytes + kEpiStageBytes);
   volatile int* abort = &bars->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -189,9 +193,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
+    // Each warp reads a 32x32 FP32 block (its 32 TMEM lanes = C rows, 32
+    // columns) per chunk, transposes it through a padded shared buffer and
+    // writes it row by row with lanes across columns: 128-byte coalesced
+    // stores for any ldc (thread-per-row stores would touch 32 rows per
+    // instruction).
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
-    const int row_in_tile = quarter * 32 + lane;
-    const bool vec_ok = (ldc % 4 == 0) && aligned16(c);
+    float* stage = epi_stage + (warp - 2) * 32 * kStagePitch;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < grid.tiles; t += gridDim.x) {
@@ -201,27 +209,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tc_fence_after();
       int mb, nb;
       grid.coords(t, mb, nb);
-      const int row = mb * kBM + row_in_tile;
-      float* crow = c + static_cast<size_t>(row) * ldc;
+      const int row0 = mb * kBM + quarter * 32;
 #pragma unroll 1
       for (int chunk = 0; chunk < kBN / 32; ++chunk) {
         float v[32];
         tc::tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                           acc * kBN + chunk * 32,
                       v);
-        const int col = nb * kBN + chunk * 32;
-        if (row < m && col < n) {
-          if (vec_ok && col + 32 <= n) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              st_stream(reinterpret_cast<float4*>(crow + col + i),
-                        make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col + i < n) crow[col + i] = v[i];
-          }
+        for (int i = 0; i < 32; ++i) stage[lane * kStagePitch + i] = v[i];
+        __syncwarp();
+        const int col = nb * kBN + chunk * 32 + lane;
+        if (col < n) {
+          const int rows = min(32, m - row0);
+#pragma unroll 4
+          for (int rr = 0; rr < rows; ++rr)
+            st_stream(c + static_cast<size_t>(row0 + rr) * ldc + col,
+                      stage[rr * kStagePitch + lane]);
         }
+        __syncwarp();
       }
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->tmem_empty[acc]);
@@ -236,25 +242,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem_base, kTmemCols);
 }
 
-// Zero-padded copy of a rows x cols FP16 matrix into a prow x pcol buffer
-// (pcol a multiple of 8 so every row starts 16-byte aligned for TMA).  One
-// CTA row-strides over destination rows; each thread assembles 8 halves and
-// writes them as one 16-byte store.
+// Eight halves starting at half `o` (0..7) of the 16 halves in w[0..7]
+// (little endian: half 2k is the low 16 bits of w[k]).
+__device__ __forceinline__ uint4 halves_at(const uint32_t (&w)[8], int o) {
+  uint32_t r[4];
+  switch (o) {
+#define OPL_EVEN(O)                                                   \
+  case O:                                                             \
+    r[0] = w[O / 2]; r[1] = w[O / 2 + 1]; r[2] = w[O / 2 + 2]; r[3] = w[O / 2 + 3]; \
+    break;
+#define OPL_ODD(O)                                                    \
+  case O:                                                             \
+    r[0] = __funnelshift_r(w[O / 2], w[O / 2 + 1], 16);               \
+    r[1] = __funnelshift_r(w[O / 2 + 1], w[O / 2 + 2], 16);           \
+    r[2] = __funnelshift_r(w[O / 2 + 2], w[O / 2 + 3], 16);           \
+    r[3] = __funnelshift_r(w[O / 2 + 3], w[O / 2 + 4], 16);           \
+    break;
+    OPL_EVEN(0) OPL_ODD(1) OPL_EVEN(2) OPL_ODD(3) OPL_EVEN(4) OPL_ODD(5) OPL_EVEN(6)
+    default: OPL_ODD(7)
+#undef OPL_EVEN
+#undef OPL_ODD
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// Zero-padded copy of a rows x cols FP16 matrix (any 2-byte-aligned base,
+// any row stride) into a prow x pcol buffer (pcol a multiple of 8, so every row
+// starts 16-byte aligned for TMA).  Each output group of 8 halves is built
+// from the two aligned 16-byte source words that cover it and a byte shift
+// that is fixed per row, so all loads and stores are 128-bit.
 __global__ void __launch_bounds__(256)
     pad_half_kernel(const __half* __restrict__ src, int rows, int cols,
                     __half* __restrict__ dst, int prow, int pcol) {
   const int groups = pcol / 8;
+  // Work from the 16-byte-aligned word holding the first element (inside
+  // the caller's allocation, whose base is 256-byte aligned).
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
+  const size_t lead = (addr & 15u) >> 1;  // halves before src in its word
+  const uint4* src4 = reinterpret_cast<const uint4*>(addr & ~uintptr_t(15));
+  const size_t total_chunks = (lead + static_cast<size_t>(rows) * cols + 7) / 8;
   for (int r = blockIdx.x; r < prow; r += gridDim.x) {
-    const __half* srow = src + static_cast<size_t>(r) * cols;
     uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
+    const size_t row_h = lead + static_cast<size_t>(r) * cols;
+    const int o = static_cast<int>(row_h & 7);
     for (int g = threadIdx.x; g < groups; g += blockDim.x) {
-      __align__(16) __half v[8];
+      uint4 out = make_uint4(0, 0, 0, 0);
+      if (r < rows && g * 8 < cols) {
+        const size_t c0 = (row_h + static_cast<size_t>(g) * 8) >> 3;
+        const uint4 lo = __ldg(src4 + c0);
+        const uint4 hi = c0 + 1 < total_chunks ? __ldg(src4 + c0 + 1) : make_uint4(0, 0, 0, 0);
+        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        out = halves_at(w, o);
+        const int valid = cols - g * 8;  // halves of this group inside the row
+        if (valid < 8) {
+          uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int col = g * 8 + i;
-        v[i] = (r < rows && col < cols) ? srow[col] : __float2half(0.0f);
+          for (int i = 0; i < 4; ++i) {
+            if (2 * i >= valid) ow[i] = 0;
+            else if (2 * i + 1 >= valid) ow[i] &= 0xffffu;
+          }
+        }
       }
-      drow[g] = *reinterpret_cast<const uint4*>(v);
+      drow[g] = out;
     }
   }
 }
