@@ -56,9 +56,28 @@ struct Barriers {
   int abort;
 };
 
+// Work units: tiles [0, tiles_full) whole; each remaining tail tile as two
+// K halves (2 units), so the last wave is two half-length passes instead of
+// one mostly idle full one.  Split units add into C (zeroed beforehand).
 struct TileGrid {
-  int m_blocks, n_blocks, tiles;
-  __device__ void coords(int t, int& mb, int& nb) const {
+  int m_blocks, n_blocks, tiles, tiles_full, units, k_blocks;
+  __host__ __device__ void init(int m, int n, int k, int grid_ctas, bool split_tail) {
+    m_blocks = (m + kBM - 1) / kBM;
+    n_blocks = (n + kBN - 1) / kBN;
+    tiles = m_blocks * n_blocks;
+    k_blocks = (k + kBK - 1) / kBK;
+    tiles_full = split_tail ? (tiles / grid_ctas) * grid_ctas : tiles;
+    units = tiles_full + 2 * (tiles - tiles_full);
+  }
+  __device__ void unit(int u, int& mb, int& nb, int& kb0, int& kb1, bool& split) const {
+    split = u >= tiles_full;
+    const int t = split ? tiles_full + ((u - tiles_full) >> 1) : u;
+    coords(t, mb, nb);
+    const int half = k_blocks / 2;
+    kb0 = split && ((u - tiles_full) & 1) ? half : 0;
+    kb1 = split && !((u - tiles_full) & 1) ? half : k_blocks;
+  }
+  __host__ __device__ void coords(int t, int& mb, int& nb) const {
     const int per_group = kGroupM * n_blocks;
     const int group = t / per_group;
     const int first_m = group * kGroupM;
@@ -72,7 +91,7 @@ struct TileGrid {
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
                    const __grid_constant__ CUtensorMap map_b, float* __restrict__ c,
-                   int m, int n, int k, int ldc, int* watchdog) {
+                   int m, int n, int k, int ldc, int split_tail, int* watchdog) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -83,10 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   TileGrid grid;
-  grid.m_blocks = (m + kBM - 1) / kBM;
-  grid.n_blocks = (n + kBN - 1) / kBN;
-  grid.tiles = grid.m_blocks * grid.n_blocks;
-  const int k_blocks = (k + kBK - 1) / kBK;
+  grid.init(m, n, k, gridDim.x, split_tail != 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -114,10 +130,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     uint32_t issued_mask = 0, issued_parity = 0;
-    for (int t = blockIdx.x; t < grid.tiles && !*abort; t += gridDim.x) {
-      int mb, nb;
-      grid.coords(t, mb, nb);
-      for (int kb = 0; kb < k_blocks; ++kb) {
+    for (int u = blockIdx.x; u < grid.units && !*abort; u += gridDim.x) {
+      int mb, nb, kb0, kb1;
+      bool split;
+      grid.unit(u, mb, nb, kb0, kb1, split);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc::mbar_wait(&bars->empty[stage], phase ^ 1, abort, watchdog,
                            tc::kWatchdogGemm))
           break;
@@ -152,13 +169,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     bool issued_any = false;
-    for (int t = blockIdx.x; t < grid.tiles && !*abort; t += gridDim.x) {
+    for (int u = blockIdx.x; u < grid.units && !*abort; u += gridDim.x) {
+      int mb, nb, kb0, kb1;
+      bool split;
+      grid.unit(u, mb, nb, kb0, kb1, split);
       if (!tc::mbar_wait(&bars->tmem_empty[acc], acc_phase ^ 1, abort, watchdog,
                          tc::kWatchdogGemm))
         break;
       tc::tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * kBN;
-      for (int kb = 0; kb < k_blocks; ++kb) {
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!tc::mbar_wait(&bars->full[stage], phase, abort, watchdog, tc::kWatchdogGemm))
           break;
         tc::tc_fence_after();
@@ -171,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // K step is two 8-row groups (2 KB).
           const uint64_t a_desc = tc::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
           const uint64_t b_desc = tc::smem_desc_sw128(b_addr + kk * 2048, kBBoxBytes, 1024);
-          tc::umma_f16(d_tmem, a_desc, b_desc, kIdesc, (kb | kk) != 0);
+          tc::umma_f16(d_tmem, a_desc, b_desc, kIdesc, (kb != kb0) || (kk != 0));
         }
         issued_any = true;
         tc::umma_commit(&bars->empty[stage]);
@@ -202,13 +222,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* stage = epi_stage + (warp - 2) * 32 * kStagePitch;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < grid.tiles; t += gridDim.x) {
+    for (int u = blockIdx.x; u < grid.units; u += gridDim.x) {
       if (!tc::mbar_wait_warp(&bars->tmem_full[acc], acc_phase, abort, watchdog,
                               tc::kWatchdogGemm))
         break;
       tc::tc_fence_after();
-      int mb, nb;
-      grid.coords(t, mb, nb);
+      int mb, nb, kb0, kb1;
+      bool split;
+      grid.unit(u, mb, nb, kb0, kb1, split);
       const int row0 = mb * kBM + quarter * 32;
 #pragma unroll 1
       for (int chunk = 0; chunk < kBN / 32; ++chunk) {
@@ -222,10 +243,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int col = nb * kBN + chunk * 32 + lane;
         if (col < n) {
           const int rows = min(32, m - row0);
+          if (split) {  // half of a tail tile: add into the zeroed C
 #pragma unroll 4
-          for (int rr = 0; rr < rows; ++rr)
-            st_stream(c + static_cast<size_t>(row0 + rr) * ldc + col,
-                      stage[rr * kStagePitch + lane]);
+            for (int rr = 0; rr < rows; ++rr)
+              atomicAdd(c + static_cast<size_t>(row0 + rr) * ldc + col,
+                        stage[rr * kStagePitch + lane]);
+          } else {
+#pragma unroll 4
+            for (int rr = 0; rr < rows; ++rr)
+              st_stream(c + static_cast<size_t>(row0 + rr) * ldc + col,
+                        stage[rr * kStagePitch + lane]);
+          }
         }
         __syncwarp();
       }
@@ -240,6 +268,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   if (warp == 1) tc::tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// Zeroes the C tiles [tiles_full, tiles) that the GEMM will build from two
+// K halves added together (0 + a + b is the same in either order, so the
+// result stays deterministic).  One CTA per tile.
+__global__ void __launch_bounds__(256)
+    zero_tail_tiles_kernel(float* __restrict__ c, int m, int n, int k, int ldc,
+                           int grid_ctas) {
+  TileGrid grid;
+  grid.init(m, n, k, grid_ctas, true);
+  int mb, nb;
+  grid.coords(grid.tiles_full + blockIdx.x, mb, nb);
+  const int col = nb * kBN + threadIdx.x;  // kBN == blockDim.x
+  if (col >= n) return;
+  const int row_end = min(m, (mb + 1) * kBM);
+  for (int row = mb * kBM; row < row_end; ++row) c[static_cast<size_t>(row) * ldc + col] = 0.0f;
 }
 
 // Eight halves starting at half `o` (0..7) of the 16 halves in w[0..7]
@@ -334,8 +378,18 @@ cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, in
   const long long tiles =
       static_cast<long long>((m + kBM - 1) / kBM) * ((n + kBN - 1) / kBN);
   const int grid = static_cast<int>(tiles < sm_count() ? tiles : sm_count());
+  // Split the tail tiles in K when the last wave would run at most half full
+  // (two halves per CTA then still fit in one wave) and K is deep enough.
+  const int tail = static_cast<int>(tiles % grid);
+  const bool split_tail = tiles > grid && tail != 0 && 2 * tail <= grid &&
+                          (k + kBK - 1) / kBK >= 8;
+  if (split_tail) {
+    zero_tail_tiles_kernel<<<tail, kBN, 0, stream>>>(c, m, n, k, ldc, grid);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   gemm_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, c, m, n, k, ldc,
-                                                         watchdog_word());
+                                                         split_tail ? 1 : 0, watchdog_word());
   return cudaGetLastError();
 }
 
