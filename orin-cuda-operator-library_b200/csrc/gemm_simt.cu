@@ -2,6 +2,7 @@
 // (reference src/gemm.cu:59-216 and :440-453).
 //
 // 128x128 CTA tile, K step 8, 256 threads each owning an 8x8 register tile
+// (updated with packed FP32x2 FMAs, two independent FP32 FMAs per instruction)
 // (two 4-row by two 4-column quads, so shared-memory fragment reads are
 // conflict-free 128-bit loads).  A is stored k-major in shared memory so both
 // operands are read as float4.  Global tiles are prefetched into registers
@@ -21,6 +22,21 @@ constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kBK = 8;
 constexpr int kThreads = 256;
+
+// Packed FP32 pair arithmetic (sm_100a f32x2): one instruction performs two
+// independent IEEE FP32 FMAs, so the 8x8 register tile needs 32 issue slots
+// per K step instead of 64 -- same per-element rounding as fmaf.
+__device__ __forceinline__ uint64_t dup2(float a) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ void fma2(uint64_t& acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
 
 template <typename T>
 struct Quad {
@@ -101,11 +117,11 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int tx = tid & 15;  // column quads tx*4 and 64 + tx*4
   const int ty = tid >> 4;  // row quads ty*4 and 64 + ty*4
-  float acc[8][8];
+  uint64_t acc2[8][4];  // acc2[i][p] = columns (2p, 2p+1) of row i
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int p = 0; p < 4; ++p) acc2[i][p] = 0;  // (+0.0f, +0.0f)
 
   const int k_tiles = (k + kBK - 1) / kBK;
   fetch(0);
@@ -116,24 +132,30 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (t + 1 < k_tiles) fetch((t + 1) * kBK);
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
-      float af[8], bf[8];
+      float af[8];
       const float4 a0 = *reinterpret_cast<const float4*>(&as[buf][kk][ty * 4]);
       const float4 a1 = *reinterpret_cast<const float4*>(&as[buf][kk][64 + ty * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&bs[buf][kk][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&bs[buf][kk][64 + tx * 4]);
+      const ulonglong2 b0 = *reinterpret_cast<const ulonglong2*>(&bs[buf][kk][tx * 4]);
+      const ulonglong2 b1 = *reinterpret_cast<const ulonglong2*>(&bs[buf][kk][64 + tx * 4]);
       af[0] = a0.x; af[1] = a0.y; af[2] = a0.z; af[3] = a0.w;
       af[4] = a1.x; af[5] = a1.y; af[6] = a1.z; af[7] = a1.w;
-      bf[0] = b0.x; bf[1] = b0.y; bf[2] = b0.z; bf[3] = b0.w;
-      bf[4] = b1.x; bf[5] = b1.y; bf[6] = b1.z; bf[7] = b1.w;
+      const uint64_t bp[4] = {b0.x, b0.y, b1.x, b1.y};
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int i = 0; i < 8; ++i) {
+        const uint64_t a2 = dup2(af[i]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(af[i], bf[j], acc[i][j]);
+        for (int p = 0; p < 4; ++p) fma2(acc2[i][p], a2, bp[p]);
+      }
     }
     if (t + 1 < k_tiles) stash(buf ^ 1);
     __syncthreads();
   }
 
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int p = 0; p < 4; ++p) unpack2(acc2[i][p], acc[i][2 * p], acc[i][2 * p + 1]);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int row = block_m + (i < 4 ? ty * 4 + i : 64 + ty * 4 + (i - 4));
