@@ -1,7 +1,8 @@
 // TORCH_LIBRARY(operatorlib, ...) binding of the B200 operator library.
 //
 // Drop-in for the reference binding python/operatorlib_binding.cpp:190-206:
-// the six schemas are identical, only the CUDA dispatch key is registered,
+// the six schemas are identical; the CUDA dispatch key runs the kernels (and,
+// beyond the reference, a Meta key gives shapes for FakeTensor tracing);
 // inputs must be contiguous CUDA tensors (no implicit copies), outputs are
 // allocated here, work goes on the input device's current stream under a
 // device guard, and the user-facing error texts match the reference's
@@ -22,8 +23,16 @@ namespace {
 
 using at::Tensor;
 
+// Meta (shape-only) calls run the same checks minus the device check.
+thread_local bool g_meta_call = false;
+
+struct MetaCall {
+  MetaCall() { g_meta_call = true; }
+  ~MetaCall() { g_meta_call = false; }
+};
+
 void require_cuda_contiguous(const Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  if (!g_meta_call) TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
 }
 
@@ -59,6 +68,7 @@ Tensor op_reduce_sum(const Tensor& input) {
   TORCH_CHECK(input.scalar_type() == at::kFloat,
               "reduce_sum supports float32 input only");
   TORCH_CHECK(input.numel() > 0, "input must be non-empty");
+  if (g_meta_call) return at::empty({}, input.options());
   c10::cuda::CUDAGuard guard(input.device());
   Tensor out = at::empty({}, input.options());
   raise_on_error(operatorlib::reduce_sum_f32(
@@ -75,6 +85,7 @@ Tensor op_softmax(const Tensor& input) {
   TORCH_CHECK(input.dim() >= 1, "input must have at least one dimension");
   const int cols = as_positive_int(input.size(-1), "last dimension");
   const int rows = as_positive_int(input.numel() / input.size(-1), "row count");
+  if (g_meta_call) return at::empty_like(input);
   c10::cuda::CUDAGuard guard(input.device());
   Tensor out = at::empty_like(input);
   raise_on_error(operatorlib::softmax_f32(input.data_ptr<float>(),
@@ -91,6 +102,7 @@ Tensor op_transpose(const Tensor& input) {
   TORCH_CHECK(input.dim() == 2, "input must be a 2D matrix");
   const int rows = as_positive_int(input.size(0), "rows");
   const int cols = as_positive_int(input.size(1), "cols");
+  if (g_meta_call) return at::empty({cols, rows}, input.options());
   c10::cuda::CUDAGuard guard(input.device());
   Tensor out = at::empty({cols, rows}, input.options());
   raise_on_error(operatorlib::transpose_f32(input.data_ptr<float>(),
@@ -115,6 +127,7 @@ Tensor op_rmsnorm(const Tensor& input, const Tensor& weight, double epsilon) {
               "weight length must equal the input hidden size");
   const int tokens =
       as_positive_int(input.numel() / input.size(-1), "token count");
+  if (g_meta_call) return at::empty_like(input);
   c10::cuda::CUDAGuard guard(input.device());
   Tensor out = at::empty_like(input);
   raise_on_error(operatorlib::rmsnorm_f32(
@@ -136,6 +149,7 @@ Tensor op_gemm(const Tensor& a, const Tensor& b) {
   const int m = as_positive_int(a.size(0), "M");
   const int k = as_positive_int(a.size(1), "K");
   const int n = as_positive_int(b.size(1), "N");
+  if (g_meta_call) return at::empty({m, n}, a.options().dtype(at::kFloat));
   c10::cuda::CUDAGuard guard(a.device());
   Tensor c = at::empty({m, n}, a.options().dtype(at::kFloat));
   const cudaError_t status =
@@ -168,6 +182,7 @@ Tensor op_attention(const Tensor& q, const Tensor& k, const Tensor& v,
   TORCH_CHECK(static_cast<int64_t>(batch) * heads <=
                   std::numeric_limits<int>::max(),
               "batch * heads exceeds the supported int32 range");
+  if (g_meta_call) return at::empty(q.sizes(), q.options().dtype(at::kFloat));
   c10::cuda::CUDAGuard guard(q.device());
   Tensor out = at::empty(q.sizes(), q.options().dtype(at::kFloat));
   const cudaError_t status =
@@ -181,6 +196,34 @@ Tensor op_attention(const Tensor& q, const Tensor& k, const Tensor& v,
                                        sequence, head_dim, causal, stream_of(q));
   raise_on_error(status, "attention");
   return out;
+}
+
+// Meta kernels: output shape/dtype only, after the same argument checks, so
+// FakeTensor tracing (torch.compile, torch.export) sees the ops.  The
+// reference registers the CUDA key only.
+Tensor meta_reduce_sum(const Tensor& input) {
+  MetaCall meta;
+  return op_reduce_sum(input);
+}
+Tensor meta_softmax(const Tensor& input) {
+  MetaCall meta;
+  return op_softmax(input);
+}
+Tensor meta_transpose(const Tensor& input) {
+  MetaCall meta;
+  return op_transpose(input);
+}
+Tensor meta_rmsnorm(const Tensor& input, const Tensor& weight, double epsilon) {
+  MetaCall meta;
+  return op_rmsnorm(input, weight, epsilon);
+}
+Tensor meta_gemm(const Tensor& a, const Tensor& b) {
+  MetaCall meta;
+  return op_gemm(a, b);
+}
+Tensor meta_attention(const Tensor& q, const Tensor& k, const Tensor& v, bool causal) {
+  MetaCall meta;
+  return op_attention(q, k, v, causal);
 }
 
 }  // namespace
@@ -201,4 +244,13 @@ TORCH_LIBRARY_IMPL(operatorlib, CUDA, m) {
   m.impl("rmsnorm", &op_rmsnorm);
   m.impl("gemm", &op_gemm);
   m.impl("attention", &op_attention);
+}
+
+TORCH_LIBRARY_IMPL(operatorlib, Meta, m) {
+  m.impl("reduce_sum", &meta_reduce_sum);
+  m.impl("softmax", &meta_softmax);
+  m.impl("transpose", &meta_transpose);
+  m.impl("rmsnorm", &meta_rmsnorm);
+  m.impl("gemm", &meta_gemm);
+  m.impl("attention", &meta_attention);
 }
