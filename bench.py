@@ -501,6 +501,23 @@ def extras(args, dist, dev, peaks, only: set[str]):
         record(name, ms, 2.0 * m * n * k, "tensor" if dtype == np.float16 else "ffma",
                peak, "TFLOP/s", world_units=dist.world)
 
+    # skinny FP16 GEMM (decode shapes, BASELINE-adjacent SURVEY row F1):
+    # bound by streaming B, reported as GB/s of A + B + C
+    if want("gemv"):
+        for m in (1, 16):
+            n = k = 4096
+            a = t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float16))
+            bs = [t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16))
+                  for _ in range(_rotations(2 * k * n))]
+            cc = torch.empty((m, n), device=dev)
+            ms = _measure(lambda i, h: lib.opl_gemm_f16(a.data_ptr(), bs[i % len(bs)].data_ptr(),
+                                                        cc.data_ptr(), m, n, k, h),
+                          steps, warm, dist, stream)
+            record(f"gemm_f16_m{m}_4096x4096", ms, 2 * (m * k + k * n) + 4 * m * n, "hbm", hbm,
+                   "GB/s", note=f"{2.0 * m * n * k / (ms * 1e-3) / 1e12:.2f} TFLOP/s",
+                   world_units=dist.world)
+        del bs
+
     # attention B1 H12 S1024 D128, FP16 and FP32, causal and not
     for dtype in (np.float16, np.float32):
         tag = "f16" if dtype == np.float16 else "f32"

@@ -16,4 +16,11 @@ cudaError_t gemm_simt(const T* a, const T* b, float* c, int m, int n, int k,
 cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n,
                         int k, cudaStream_t stream);
 
+// Skinny FP16 GEMM for M <= 16 (bandwidth-bound on B): split-K SIMT kernel
+// with a fixed-order reduction; gemv_f16_supported says whether it applies
+// (N % 8 == 0, 16-byte aligned B and C).
+bool gemv_f16_supported(const void* b, const void* c, int m, int n);
+cudaError_t gemv_f16(const __half* a, const __half* b, float* c, int m, int n, int k,
+                     cudaStream_t stream);
+
 }  // namespace opl

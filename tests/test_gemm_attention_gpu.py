@@ -192,3 +192,23 @@ def test_gemm_f16_deterministic(cuda, stream, m, n, k):
     idx = np.unique(np.linspace(0, m - 1, 40).astype(int))
     want = a.cpu().numpy()[idx].astype(np.float64) @ b.cpu().numpy().astype(np.float64)
     check_f16(outs[0].cpu().numpy()[idx], want)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (2, 1000, 4096), (3, 4104, 333), (8, 2048, 2048),
+                                   (16, 4096, 4096), (16, 8, 7), (5, 8192, 64), (1, 64, 100_000)])
+def test_gemm_f16_skinny(cuda, stream, m, n, k):
+    """Decode-style M <= 16 (split-K SIMT path, fixed-order reduction):
+    FP16 gates and bit-identical repeat runs."""
+    import torch
+
+    rng = np.random.default_rng(m * 7 + n + k)
+    a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float16)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16)
+    ad, bd = dev(a, cuda), dev(b, cuda)
+    c1 = torch.empty((m, n), device=cuda)
+    c2 = torch.empty((m, n), device=cuda)
+    operatorlib.gemm_into(ad, bd, c1)
+    operatorlib.gemm_into(ad, bd, c2)
+    stream.synchronize()
+    assert torch.equal(c1, c2)
+    check_f16(c1.cpu().numpy(), a.astype(np.float64) @ b.astype(np.float64))
