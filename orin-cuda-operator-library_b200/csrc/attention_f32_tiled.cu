@@ -1,0 +1,262 @@
+// FP32 flash-attention forward on FFMA, tiled like an SGEMM, for head_dim 64
+// or 128 (reference src/attention.cu:51-150 and :445-484, there one warp per
+// query row with a shuffle-reduced dot product per key).
+//
+// CTA = (batch*head, 128 query rows), 256 threads; thread (tr, tc) with
+// tr = tid / 16 (0..15), tc = tid % 16 owns query rows 8*tr .. 8*tr+7 in both
+// phases, so its running max / denominator stay in registers:
+//   S phase   S[8 rows][4 keys] (keys 4*tc..) over D: per d one 8-row Q
+//             fragment (Q stored d-major in shared memory, two 128-bit loads)
+//             and one 4-key K fragment (K stored d-major, one 128-bit load);
+//   softmax   row max / sum across the 16 lanes of a row group (xor
+//             shuffles), online rescaling of O;
+//   PV phase  O[8 rows][D/16 columns] += P V over the 64 keys: P stored
+//             key-major (8-row fragment = two 128-bit loads), V row-major.
+// Register-tile updates use packed fma.rn.f32x2 (two independent FP32 FMAs
+// per instruction, same rounding as fmaf).  Causal tiles past the diagonal
+// are skipped; the grid starts with the longest (bottom) query blocks.
+#include "attention_simt.cuh"
+
+namespace opl {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 64;
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ uint64_t dup2f(float a) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(a));
+  return r;
+}
+__device__ __forceinline__ uint64_t pack2f(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void fma2f(uint64_t& acc, uint64_t a, uint64_t b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ void unpack2f(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+template <int D>
+struct F32Cfg {
+  static constexpr int kQPitch = kBM + 4;   // Qt[d][row]
+  static constexpr int kKPitch = kBN + 4;   // Kt[d][key]
+  static constexpr int kVPitch = D + 4;     // V[key][d]
+  static constexpr int kPPitch = kBM + 4;   // Pt[key][row]
+  static constexpr int kCols = D / 16;      // output columns per thread
+  static constexpr size_t kSmemFloats = static_cast<size_t>(D) * kQPitch +
+                                        static_cast<size_t>(D) * kKPitch +
+                                        static_cast<size_t>(kBN) * kVPitch +
+                                        static_cast<size_t>(kBN) * kPPitch;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_f32_tiled_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                               const float* __restrict__ v, float* __restrict__ out,
+                               int heads_total, int seq, int causal, float scale) {
+  using Cfg = F32Cfg<D>;
+  extern __shared__ __align__(16) float smem[];
+  float* qt = smem;                              // [D][kQPitch]
+  float* kt = qt + D * Cfg::kQPitch;             // [D][kKPitch]
+  float* vs = kt + D * Cfg::kKPitch;             // [kBN][kVPitch]
+  float* pt = vs + kBN * Cfg::kVPitch;           // [kBN][kPPitch]
+
+  const int q_blocks = (seq + kBM - 1) / kBM;
+  const int bh = blockIdx.x % heads_total;
+  const int qb = q_blocks - 1 - static_cast<int>(blockIdx.x / heads_total);
+  const int q0 = qb * kBM;
+  const size_t base = static_cast<size_t>(bh) * seq * D;
+  const int tid = threadIdx.x;
+  const int tr = tid >> 4;
+  const int tc = tid & 15;
+
+  // Q tile -> d-major shared copy (rows past S are zero).
+  for (int idx = tid; idx < kBM * (D / 4); idx += kThreads) {
+    const int row = idx % kBM;
+    const int c4 = idx / kBM;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + row < seq)
+      x = __ldg(reinterpret_cast<const float4*>(q + base + static_cast<size_t>(q0 + row) * D) + c4);
+    qt[(4 * c4 + 0) * Cfg::kQPitch + row] = x.x;
+    qt[(4 * c4 + 1) * Cfg::kQPitch + row] = x.y;
+    qt[(4 * c4 + 2) * Cfg::kQPitch + row] = x.z;
+    qt[(4 * c4 + 3) * Cfg::kQPitch + row] = x.w;
+  }
+
+  float m_run[8], l_run[8];
+  uint64_t o2[8][Cfg::kCols / 2];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < Cfg::kCols / 2; ++c) o2[i][c] = 0;
+  }
+
+  const int q_last = min(q0 + kBM, seq) - 1;
+  const int key_end = causal ? q_last + 1 : seq;
+  for (int k0 = 0; k0 < key_end; k0 += kBN) {
+    __syncthreads();  // previous tile consumed (and Q written on the first pass)
+    for (int idx = tid; idx < kBN * (D / 4); idx += kThreads) {
+      const int key = idx % kBN;
+      const int c4 = idx / kBN;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + key < seq)
+        x = __ldg(reinterpret_cast<const float4*>(k + base + static_cast<size_t>(k0 + key) * D) + c4);
+      kt[(4 * c4 + 0) * Cfg::kKPitch + key] = x.x;
+      kt[(4 * c4 + 1) * Cfg::kKPitch + key] = x.y;
+      kt[(4 * c4 + 2) * Cfg::kKPitch + key] = x.z;
+      kt[(4 * c4 + 3) * Cfg::kKPitch + key] = x.w;
+    }
+    for (int idx = tid; idx < kBN * (D / 4); idx += kThreads) {
+      const int key = idx / (D / 4);
+      const int c4 = idx % (D / 4);
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k0 + key < seq)
+        x = __ldg(reinterpret_cast<const float4*>(v + base + static_cast<size_t>(k0 + key) * D) + c4);
+      *reinterpret_cast<float4*>(&vs[key * Cfg::kVPitch + 4 * c4]) = x;
+    }
+    __syncthreads();
+
+    // S = Q K^T for rows 8tr.., keys 4tc..: s2[i][0..1] hold key pairs.
+    uint64_t s2[8][2];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s2[i][0] = s2[i][1] = 0;
+#pragma unroll 4
+    for (int d = 0; d < D; ++d) {
+      const float4 qa = *reinterpret_cast<const float4*>(&qt[d * Cfg::kQPitch + tr * 8]);
+      const float4 qb4 = *reinterpret_cast<const float4*>(&qt[d * Cfg::kQPitch + tr * 8 + 4]);
+      const ulonglong2 kk = *reinterpret_cast<const ulonglong2*>(&kt[d * Cfg::kKPitch + tc * 4]);
+      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb4.x, qb4.y, qb4.z, qb4.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint64_t a = dup2f(qv[i]);
+        fma2f(s2[i][0], a, kk.x);
+        fma2f(s2[i][1], a, kk.y);
+      }
+    }
+
+    // Online softmax per row; the 16 lanes sharing tr hold the row's 64 keys.
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = q0 + tr * 8 + i;
+      float s[4];
+      unpack2f(s2[i][0], s[0], s[1]);
+      unpack2f(s2[i][1], s[2], s[3]);
+      float tile_max = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int key = k0 + tc * 4 + j;
+        const bool valid = key < seq && (!causal || key <= row);
+        s[j] = valid ? s[j] * scale : -INFINITY;
+        tile_max = fmaxf(tile_max, s[j]);
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1)
+        tile_max = fmaxf(tile_max, __shfl_xor_sync(kFullMask, tile_max, o));
+      const float m_new = fmaxf(m_run[i], tile_max);
+      const float alpha = (m_new == -INFINITY) ? 1.0f : expf(m_run[i] - m_new);
+      float tile_sum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        s[j] = (s[j] == -INFINITY) ? 0.0f : expf(s[j] - m_new);
+        tile_sum += s[j];
+      }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) tile_sum += __shfl_xor_sync(kFullMask, tile_sum, o);
+      l_run[i] = l_run[i] * alpha + tile_sum;
+      m_run[i] = m_new;
+      const uint64_t a2 = dup2f(alpha);
+#pragma unroll
+      for (int c = 0; c < Cfg::kCols / 2; ++c) {
+        uint64_t scaled = 0;
+        fma2f(scaled, o2[i][c], a2);
+        o2[i][c] = scaled;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pt[(tc * 4 + j) * Cfg::kPPitch + tr * 8 + i] = s[j];
+    }
+    __syncthreads();
+
+    // O += P V over this tile's keys.
+    const int key_count = min(kBN, seq - k0);
+#pragma unroll 2
+    for (int j = 0; j < key_count; ++j) {
+      const float4 pa = *reinterpret_cast<const float4*>(&pt[j * Cfg::kPPitch + tr * 8]);
+      const float4 pb = *reinterpret_cast<const float4*>(&pt[j * Cfg::kPPitch + tr * 8 + 4]);
+      const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+      uint64_t vv[Cfg::kCols / 2];
+      if constexpr (Cfg::kCols == 8) {
+        const ulonglong2 v0 = *reinterpret_cast<const ulonglong2*>(&vs[j * Cfg::kVPitch + tc * 8]);
+        const ulonglong2 v1 = *reinterpret_cast<const ulonglong2*>(&vs[j * Cfg::kVPitch + tc * 8 + 4]);
+        vv[0] = v0.x; vv[1] = v0.y; vv[2] = v1.x; vv[3] = v1.y;
+      } else {
+        const ulonglong2 v0 = *reinterpret_cast<const ulonglong2*>(&vs[j * Cfg::kVPitch + tc * 4]);
+        vv[0] = v0.x; vv[1] = v0.y;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint64_t a = dup2f(pv[i]);
+#pragma unroll
+        for (int c = 0; c < Cfg::kCols / 2; ++c) fma2f(o2[i][c], a, vv[c]);
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int row = q0 + tr * 8 + i;
+    if (row >= seq) continue;
+    const float inv = 1.0f / l_run[i];
+    float* orow = out + base + static_cast<size_t>(row) * D + tc * Cfg::kCols;
+#pragma unroll
+    for (int c = 0; c < Cfg::kCols / 2; c += 2) {
+      float a0, a1, b0, b1;
+      unpack2f(o2[i][c], a0, a1);
+      unpack2f(o2[i][c + 1], b0, b1);
+      *reinterpret_cast<float4*>(orow + 2 * c) = make_float4(a0 * inv, a1 * inv, b0 * inv, b1 * inv);
+    }
+  }
+}
+
+template <int D>
+cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, float* out,
+                             int heads_total, int seq, bool causal, cudaStream_t stream) {
+  using Cfg = F32Cfg<D>;
+  const size_t smem = Cfg::kSmemFloats * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(attention_f32_tiled_kernel<D>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const long long ctas = static_cast<long long>(heads_total) * ((seq + kBM - 1) / kBM);
+  if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+  attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
+      q, k, v, out, heads_total, seq, causal ? 1 : 0, 1.0f / sqrtf(static_cast<float>(D)));
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool attention_f32_tiled_supported(int head_dim, const void* q, const void* k, const void* v,
+                                   const void* out) {
+  return (head_dim == 64 || head_dim == 128) && aligned16(q) && aligned16(k) &&
+         aligned16(v) && aligned16(out);
+}
+
+cudaError_t attention_f32_tiled(const float* q, const float* k, const float* v, float* out,
+                                int batch, int heads, int seq, int head_dim, bool causal,
+                                cudaStream_t stream) {
+  const long long total = static_cast<long long>(batch) * heads;
+  if (total > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (head_dim == 128)
+    return launch_f32_tiled<128>(q, k, v, out, static_cast<int>(total), seq, causal, stream);
+  return launch_f32_tiled<64>(q, k, v, out, static_cast<int>(total), seq, causal, stream);
+}
+
+}  // namespace opl

@@ -222,6 +222,9 @@ extern "C" int opl_attention_f32(const float* q, const float* k, const float* v,
       batch <= 0 || heads <= 0 || sequence <= 0 || head_dim <= 0 ||
       head_dim > 128)
     return cudaErrorInvalidValue;
+  if (opl::attention_f32_tiled_supported(head_dim, q, k, v, output))
+    return opl::attention_f32_tiled(q, k, v, output, batch, heads, sequence, head_dim,
+                                    causal != 0, stream);
   return opl::attention_simt<float>(q, k, v, output, batch, heads, sequence,
                                     head_dim, causal != 0, stream);
 }
