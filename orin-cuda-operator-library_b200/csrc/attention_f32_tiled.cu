@@ -14,7 +14,9 @@
 //             key-major (8-row fragment = two 128-bit loads), V row-major.
 // Register-tile updates use packed fma.rn.f32x2 (two independent FP32 FMAs
 // per instruction, same rounding as fmaf).  Causal tiles past the diagonal
-// are skipped; the grid starts with the longest (bottom) query blocks.
+// are skipped; the grid starts with the longest (bottom) query blocks.  When
+// (head, query block) units would leave SMs idle, the KV range is split across
+// CTAs and attention_combine_kernel merges the partial results.
 #include "attention_simt.cuh"
 
 namespace opl {
@@ -59,7 +61,9 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_f32_tiled_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                const float* __restrict__ v, float* __restrict__ out,
-                               int heads_total, int seq, int causal, float scale) {
+                               int heads_total, int seq, int causal, float scale,
+                               int splits, float* __restrict__ part_o,
+                               float2* __restrict__ part_ml) {
   using Cfg = F32Cfg<D>;
   extern __shared__ __align__(16) float smem[];
   float* qt = smem;                              // [D][kQPitch]
@@ -68,8 +72,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* pt = vs + kBN * Cfg::kVPitch;           // [kBN][kPPitch]
 
   const int q_blocks = (seq + kBM - 1) / kBM;
-  const int bh = blockIdx.x % heads_total;
-  const int qb = q_blocks - 1 - static_cast<int>(blockIdx.x / heads_total);
+  const int sp = blockIdx.x % splits;
+  const int rest = blockIdx.x / splits;
+  const int bh = rest % heads_total;
+  const int qb = q_blocks - 1 - rest / heads_total;
   const int q0 = qb * kBM;
   const size_t base = static_cast<size_t>(bh) * seq * D;
   const int tid = threadIdx.x;
@@ -100,8 +106,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   const int q_last = min(q0 + kBM, seq) - 1;
-  const int key_end = causal ? q_last + 1 : seq;
-  for (int k0 = 0; k0 < key_end; k0 += kBN) {
+  const int key_total = causal ? q_last + 1 : seq;
+  // This CTA's share of the KV tiles (all of them when splits == 1).
+  const int kv_tiles = (key_total + kBN - 1) / kBN;
+  const int chunk = (kv_tiles + splits - 1) / splits;
+  const int key_begin = min(sp * chunk, kv_tiles) * kBN;
+  const int key_end = min(min((sp + 1) * chunk, kv_tiles) * kBN, key_total);
+  for (int k0 = key_begin; k0 < key_end; k0 += kBN) {
     __syncthreads();  // previous tile consumed (and Q written on the first pass)
     for (int idx = tid; idx < kBN * (D / 4); idx += kThreads) {
       const int key = idx % kBN;
@@ -209,6 +220,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if (splits > 1) {
+    // Partial result of this KV chunk: unnormalised O with its (m, l);
+    // attention_combine_kernel merges the chunks.  An empty chunk leaves
+    // m = -inf, l = 0, O = 0.
+    const size_t slice = static_cast<size_t>(heads_total) * seq;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int row = q0 + tr * 8 + i;
+      if (row >= seq) continue;
+      const size_t r_index = static_cast<size_t>(sp) * slice + static_cast<size_t>(bh) * seq + row;
+      if (tc == 0) part_ml[r_index] = make_float2(m_run[i], l_run[i]);
+      float* orow = part_o + r_index * D + tc * Cfg::kCols;
+#pragma unroll
+      for (int c = 0; c < Cfg::kCols / 2; c += 2) {
+        float a0, a1, b0, b1;
+        unpack2f(o2[i][c], a0, a1);
+        unpack2f(o2[i][c + 1], b0, b1);
+        *reinterpret_cast<float4*>(orow + 2 * c) = make_float4(a0, a1, b0, b1);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int row = q0 + tr * 8 + i;
@@ -225,6 +258,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+}  // namespace
+
+// Merges split-KV partial results: per (head, row), m = max_s m_s,
+// l = sum_s l_s e^(m_s - m), O = sum_s O_s e^(m_s - m) / l, splits added in
+// order s = 0, 1, ... (deterministic).  One warp per row, D/32 floats per
+// lane.  `log2_domain` selects 2^x (tensor-core kernel) instead of e^x.
+__global__ void __launch_bounds__(256)
+    attention_combine_kernel(const float* __restrict__ part_o,
+                             const float2* __restrict__ part_ml, float* __restrict__ out,
+                             size_t rows, int d, int splits, int log2_domain) {
+  const size_t row = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float m = -INFINITY;
+  for (int s = 0; s < splits; ++s) m = fmaxf(m, part_ml[static_cast<size_t>(s) * rows + row].x);
+  float l = 0.0f;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < splits; ++s) {
+    const float2 ml = part_ml[static_cast<size_t>(s) * rows + row];
+    if (ml.x == -INFINITY) continue;  // empty chunk
+    const float w = log2_domain ? exp2f(ml.x - m) : expf(ml.x - m);
+    l += ml.y * w;
+    const float* o = part_o + (static_cast<size_t>(s) * rows + row) * d;
+    for (int c = lane, i = 0; c < d; c += 32, ++i) acc[i] += o[c] * w;
+  }
+  const float inv = 1.0f / l;
+  float* orow = out + row * d;
+  for (int c = lane, i = 0; c < d; c += 32, ++i) orow[c] = acc[i] * inv;
+}
+
+namespace {
+
 template <int D>
 cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, float* out,
                              int heads_total, int seq, bool causal, cudaStream_t stream) {
@@ -234,11 +299,40 @@ cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, flo
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
-  const long long ctas = static_cast<long long>(heads_total) * ((seq + kBM - 1) / kBM);
+  const long long units = static_cast<long long>(heads_total) * ((seq + kBM - 1) / kBM);
+  // Split the KV range across CTAs when the grid would leave SMs idle (and
+  // to spread the long bottom rows of causal grids): about two CTAs per SM,
+  // at least two KV tiles per chunk.
+  const int kv_tiles = (seq + kBN - 1) / kBN;
+  int splits = 1;
+  if (units < sm_count()) {
+    splits = static_cast<int>((2LL * sm_count() + units - 1) / units);
+    splits = max(1, min(splits, kv_tiles / 2));
+  }
+  const long long ctas = units * splits;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  if (splits == 1) {
+    attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
+        q, k, v, out, heads_total, seq, causal ? 1 : 0, scale, 1, nullptr, nullptr);
+    return cudaGetLastError();
+  }
+  const size_t rows = static_cast<size_t>(heads_total) * seq;
+  void* ws = nullptr;
+  e = cudaMallocAsync(&ws, rows * splits * (D * sizeof(float) + sizeof(float2)), stream);
+  if (e != cudaSuccess) return e;
+  float* part_o = static_cast<float*>(ws);
+  float2* part_ml = reinterpret_cast<float2*>(part_o + rows * splits * D);
   attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
-      q, k, v, out, heads_total, seq, causal ? 1 : 0, 1.0f / sqrtf(static_cast<float>(D)));
-  return cudaGetLastError();
+      q, k, v, out, heads_total, seq, causal ? 1 : 0, scale, splits, part_o, part_ml);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) {
+    attention_combine_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
+        part_o, part_ml, out, rows, D, splits, 0);
+    e = cudaGetLastError();
+  }
+  const cudaError_t f = cudaFreeAsync(ws, stream);
+  return e != cudaSuccess ? e : f;
 }
 
 }  // namespace
