@@ -464,11 +464,15 @@ def extras(args, dist, dev, peaks, only: set[str]):
         if dist.world == 1:
             ms = _measure(lambda i, hh: lib.opl_reduce_sum_f32(xs[i % len(xs)].data_ptr(), res.data_ptr(), n, hh),
                           steps, warm, dist, stream)
-        else:  # local FP64 partial + NCCL all-reduce (eager launches)
-            def call(i):
-                assert lib.opl_reduce_sum_partial_f64(xs[i % len(xs)].data_ptr(), part.data_ptr(), n, h) == 0
+        else:  # local FP64 partial + NCCL FP64 all-reduce, captured together
+            def call(i, hh):
+                rc = lib.opl_reduce_sum_partial_f64(xs[i % len(xs)].data_ptr(), part.data_ptr(), n, hh)
                 dist.pg.all_reduce(part)
-            ms = _measure(call, steps, warm, dist, stream, graph=False)
+                return rc
+            try:
+                ms = _measure(call, steps, warm, dist, stream)
+            except Exception:  # NCCL without graph-capture support: eager launches
+                ms = _measure(lambda i: call(i, h), steps, warm, dist, stream, graph=False)
         record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world)
 
     # ragged row ops 4097x1023
