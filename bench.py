@@ -464,7 +464,18 @@ def extras(args, dist, dev, peaks, only: set[str]):
         if dist.world == 1:
             ms = _measure(lambda i, hh: lib.opl_reduce_sum_f32(xs[i % len(xs)].data_ptr(), res.data_ptr(), n, hh),
                           steps, warm, dist, stream)
-        else:  # local FP64 partial + NCCL FP64 all-reduce, captured together
+        else:
+            # Fused: partial sums exchanged over NVLink peer memory inside the
+            # reduce's finalize kernel (operatorlib.ReduceTeam).
+            import operatorlib as _ol
+
+            team = _ol.ReduceTeam(dist.rank, dist.world)
+            ms = _measure(lambda i, hh: team.launch(xs[i % len(xs)], res, hh), steps, warm,
+                          dist, stream)
+            record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world,
+                   note="fused: per-GPU FP64 partial + all-reduce over NVLink peer stores")
+            team.close()
+        if dist.world > 1:  # local FP64 partial + NCCL FP64 all-reduce, captured together
             def call(i, hh):
                 rc = lib.opl_reduce_sum_partial_f64(xs[i % len(xs)].data_ptr(), part.data_ptr(), n, hh)
                 dist.pg.all_reduce(part)
@@ -473,7 +484,10 @@ def extras(args, dist, dev, peaks, only: set[str]):
                 ms = _measure(call, steps, warm, dist, stream)
             except Exception:  # NCCL without graph-capture support: eager launches
                 ms = _measure(lambda i: call(i, h), steps, warm, dist, stream, graph=False)
-        record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world)
+            record("reduce_16M_nccl", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world,
+                   note="per-GPU FP64 partial + NCCL all-reduce (comparison)")
+        else:
+            record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s")
 
     # ragged row ops 4097x1023
     if want("ragged"):

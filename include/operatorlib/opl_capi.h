@@ -58,6 +58,22 @@ int opl_reduce_sum_partial_f64(const float* input, double* output, size_t n,
 int opl_reduce_sum_f32_noalloc(const float* input, float* output, size_t n,
                                opl_stream_t stream);
 
+/* Multi-GPU reduce fused with its all-reduce (no reference counterpart: the
+ * reference is single-GPU; it replaces "per-GPU reduce + NCCL all-reduce").
+ * A team is one rank per GPU of a node.  opl_team_create allocates this
+ * GPU's team buffer and returns its CUDA IPC handle (64 bytes) to share with
+ * the other ranks; opl_team_connect opens the peers' buffers from the
+ * world * 64-byte array of all handles (rank order).  Every rank then calls
+ * opl_team_reduce_sum_f32 on its own chunk, in the same order on all ranks:
+ * each GPU sums its chunk, exchanges the FP64 partial with the peers over
+ * NVLink and writes the identical total to *output.  A peer that does not
+ * arrive within a bounded wait yields NaN and the watchdog code. */
+int opl_team_create(int rank, int world, void** team, void* ipc_handle_out);
+int opl_team_connect(void* team, const void* all_ipc_handles);
+int opl_team_reduce_sum_f32(void* team, const float* input, float* output, size_t n,
+                            opl_stream_t stream);
+int opl_team_destroy(void* team);
+
 /* Replaces operatorlib::softmax_f32, operators.h:16-17 (src/softmax.cu:182-202). */
 int opl_softmax_f32(const float* input, float* output, int rows, int cols,
                     opl_stream_t stream);

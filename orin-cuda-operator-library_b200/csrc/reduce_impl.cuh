@@ -8,6 +8,11 @@ namespace opl {
 constexpr int kReduceThreads = 512;
 constexpr int kReduceCtasPerSm = 4;
 
+// Per-CTA FP64 partial sums of input[0..n) into partials[blockIdx.x]
+// (kReduceThreads threads; triggers programmatic dependent launch).
+__global__ void reduce_partials_kernel(const float* __restrict__ input, std::size_t n,
+                                       double* __restrict__ partials);
+
 // Number of partial-sum CTAs used for n elements on the current device
 // (at most sm_count() * kReduceCtasPerSm).
 int reduce_grid(std::size_t n);

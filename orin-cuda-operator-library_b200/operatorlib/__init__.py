@@ -57,6 +57,14 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = ctypes.c_int
+    lib.opl_team_create.argtypes = [i, i, ctypes.POINTER(vp), ctypes.c_char_p]
+    lib.opl_team_create.restype = ctypes.c_int
+    lib.opl_team_connect.argtypes = [vp, ctypes.c_char_p]
+    lib.opl_team_connect.restype = ctypes.c_int
+    lib.opl_team_reduce_sum_f32.argtypes = [vp, vp, vp, sz, vp]
+    lib.opl_team_reduce_sum_f32.restype = ctypes.c_int
+    lib.opl_team_destroy.argtypes = [vp]
+    lib.opl_team_destroy.restype = ctypes.c_int
     lib.opl_error_string.argtypes = [ctypes.c_int]
     lib.opl_error_string.restype = ctypes.c_char_p
     lib.opl_version.argtypes = []
@@ -112,7 +120,10 @@ from .raw import (  # noqa: E402  (re-exported convenience layer)
     transpose_into,
 )
 
+from .team import ReduceTeam  # noqa: E402
+
 __all__ = [
+    "ReduceTeam",
     "OplError", "capi", "load_operatorlib", "check", "version",
     "attention_into", "gemm_into", "reduce_sum_into",
     "reduce_sum_partial_f64_into", "rmsnorm_into", "softmax_into",
