@@ -531,6 +531,25 @@ def extras(args, dist, dev, peaks, only: set[str]):
         ms = _measure(lambda i, h: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
         record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
 
+    # 16-bit I/O row ops: BF16 softmax 4096x1024, RMSNorm 2048x4096
+    if want("row16"):
+        for tag, fn, (r, c) in [("softmax_bf16_4096x1024", lib.opl_softmax_bf16, SOFTMAX_SHAPE),
+                                ("rmsnorm_bf16_2048x4096", lib.opl_rmsnorm_bf16, RMS_SHAPE)]:
+            xs16 = [t(rng.normal(0, 1, (r, c)).astype(np.float32)).to(torch.bfloat16)
+                    for _ in range(_rotations(4 * r * c))]
+            w16 = t(rng.normal(1, 0.1, c).astype(np.float32)).to(torch.bfloat16)
+            y16 = torch.empty((r, c), device=dev, dtype=torch.bfloat16)
+            if tag.startswith("softmax"):
+                call16 = lambda i, hh: fn(xs16[i % len(xs16)].data_ptr(), y16.data_ptr(), r, c, hh)
+                work = 4 * r * c
+            else:
+                call16 = lambda i, hh: fn(xs16[i % len(xs16)].data_ptr(), w16.data_ptr(),
+                                          y16.data_ptr(), r, c, RMS_EPS, hh)
+                work = 4 * r * c + 2 * c
+            ms = _measure(call16, steps, warm, dist, stream)
+            record(tag, ms, work, "hbm", hbm, "GB/s", world_units=dist.world)
+            del xs16
+
     # GEMM 4096^3 FP16 (tensor cores), FP32 (FFMA), non-aligned FP16
     for name, dtype, (m, n, k) in [("gemm_f16_4096", np.float16, (4096, 4096, 4096)),
                                    ("gemm_f16_4095x4097x4093", np.float16, (4095, 4097, 4093)),

@@ -30,6 +30,9 @@ typedef struct CUstream_st* opl_stream_t;
 /* FP16 storage (IEEE binary16 bits), layout-compatible with __half. */
 typedef uint16_t opl_half_t;
 
+/* BF16 storage (bfloat16 bits), layout-compatible with __nv_bfloat16. */
+typedef uint16_t opl_bf16_t;
+
 /* Replaces operatorlib::reduce_sum_f32, include/operatorlib/operators.h:13-14
  * (implementation src/reduce.cu:54-69).  Sum of n floats, accumulated in
  * FP64 per block and combined in a fixed order: deterministic.  Uses a
@@ -77,6 +80,21 @@ int opl_team_destroy(void* team);
 /* Replaces operatorlib::softmax_f32, operators.h:16-17 (src/softmax.cu:182-202). */
 int opl_softmax_f32(const float* input, float* output, int rows, int cols,
                     opl_stream_t stream);
+
+/* 16-bit I/O variants of softmax_f32 and rmsnorm_f32 (no counterpart in the
+ * reference, whose launchers are FP32-only; it defers 16-bit I/O to a later
+ * interface stage, docs/standalone_benchmark.md:14-16).  Inputs, weight and
+ * outputs in FP16 or BF16; max / sums / normalisation in FP32; each result
+ * rounded once to the storage type.  Same argument checks as the FP32
+ * versions. */
+int opl_softmax_f16(const opl_half_t* input, opl_half_t* output, int rows, int cols,
+                    opl_stream_t stream);
+int opl_softmax_bf16(const opl_bf16_t* input, opl_bf16_t* output, int rows, int cols,
+                     opl_stream_t stream);
+int opl_rmsnorm_f16(const opl_half_t* input, const opl_half_t* weight, opl_half_t* output,
+                    int tokens, int hidden, float epsilon, opl_stream_t stream);
+int opl_rmsnorm_bf16(const opl_bf16_t* input, const opl_bf16_t* weight, opl_bf16_t* output,
+                     int tokens, int hidden, float epsilon, opl_stream_t stream);
 
 /* Replaces operatorlib::transpose_f32, operators.h:19-20
  * (src/transpose.cu:38-47).  Bit-exact data movement. */

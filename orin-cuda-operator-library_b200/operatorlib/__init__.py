@@ -45,6 +45,10 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "opl_reduce_sum_partial_f64": [vp, vp, sz, vp],
         "opl_reduce_sum_f32_noalloc": [vp, vp, sz, vp],
         "opl_softmax_f32": [vp, vp, i, i, vp],
+        "opl_softmax_f16": [vp, vp, i, i, vp],
+        "opl_softmax_bf16": [vp, vp, i, i, vp],
+        "opl_rmsnorm_f16": [vp, vp, vp, i, i, f, vp],
+        "opl_rmsnorm_bf16": [vp, vp, vp, i, i, f, vp],
         "opl_transpose_f32": [vp, vp, i, i, vp],
         "opl_rmsnorm_f32": [vp, vp, vp, i, i, f, vp],
         "opl_gemm_f32": [vp, vp, vp, i, i, i, vp],

@@ -41,9 +41,17 @@ def reduce_sum_partial_f64_into(x, out, stream=None) -> None:
         _ptr(x), _ptr(out), x.numel(), _stream(x, stream)))
 
 
+def _dtype_fn(base: str, dtype):
+    import torch
+
+    suffix = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}[dtype]
+    return getattr(_lib(), f"opl_{base}_{suffix}")
+
+
 def softmax_into(x, out, stream=None) -> None:
+    """FP32, FP16 or BF16 (out has x's dtype; arithmetic in FP32)."""
     cols = x.shape[-1]
-    _check("softmax", _lib().opl_softmax_f32(
+    _check("softmax", _dtype_fn("softmax", x.dtype)(
         _ptr(x), _ptr(out), x.numel() // cols, cols, _stream(x, stream)))
 
 
@@ -54,8 +62,9 @@ def transpose_into(x, out, stream=None) -> None:
 
 
 def rmsnorm_into(x, w, out, eps: float, stream=None) -> None:
+    """FP32, FP16 or BF16 (w and out have x's dtype; arithmetic in FP32)."""
     hidden = x.shape[-1]
-    _check("rmsnorm", _lib().opl_rmsnorm_f32(
+    _check("rmsnorm", _dtype_fn("rmsnorm", x.dtype)(
         _ptr(x), _ptr(w), _ptr(out), x.numel() // hidden, hidden, float(eps),
         _stream(x, stream)))
 
