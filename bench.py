@@ -936,6 +936,16 @@ def run_profile(args) -> int:
                                                        rows, cols, RMS_EPS, h),
                 "transpose": lambda: lib.opl_transpose_f32(x.data_ptr(), y.data_ptr(), rows,
                                                            cols, h)}[op]
+    elif op in ("softmax_bf16", "rmsnorm_bf16"):
+        rows, cols = shape or {"softmax_bf16": SOFTMAX_SHAPE, "rmsnorm_bf16": RMS_SHAPE}[op]
+        x = t(rng.normal(0, 1, (rows, cols)).astype(np.float32)).to(torch.bfloat16)
+        w = t(rng.normal(1, 0.1, cols).astype(np.float32)).to(torch.bfloat16)
+        y = torch.empty((rows, cols), device=dev, dtype=torch.bfloat16)
+        call = {"softmax_bf16": lambda: lib.opl_softmax_bf16(x.data_ptr(), y.data_ptr(), rows,
+                                                             cols, h),
+                "rmsnorm_bf16": lambda: lib.opl_rmsnorm_bf16(x.data_ptr(), w.data_ptr(),
+                                                             y.data_ptr(), rows, cols, RMS_EPS,
+                                                             h)}[op]
     else:
         raise SystemExit(f"unknown --profile op {op}")
     for _ in range(args.warmup + args.steps):

@@ -7,6 +7,9 @@ extern "C" int opl_gemm_f16(const opl_half_t* a, const opl_half_t* b, float* c,
                             int m, int n, int k, opl_stream_t stream) {
   if (a == nullptr || b == nullptr || c == nullptr || m <= 0 || n <= 0 || k <= 0)
     return cudaErrorInvalidValue;
+  if (opl::gemv_tc_supported(a, b, m, n, k))
+    return opl::gemv_tc(reinterpret_cast<const __half*>(a),
+                        reinterpret_cast<const __half*>(b), c, m, n, k, stream);
   if (opl::gemv_f16_supported(b, c, m, n))
     return opl::gemv_f16(reinterpret_cast<const __half*>(a),
                          reinterpret_cast<const __half*>(b), c, m, n, k, stream);

@@ -23,4 +23,12 @@ bool gemv_f16_supported(const void* b, const void* c, int m, int n);
 cudaError_t gemv_f16(const __half* a, const __half* b, float* c, int m, int n, int k,
                      cudaStream_t stream);
 
+// Skinny FP16 GEMM for M <= 128 on the tensor cores with swapped operands
+// (C^T = B^T A^T), K split across a thread-block cluster and summed through
+// distributed shared memory; needs N % 8 == 0, K % 8 == 0 and 16-byte
+// aligned A and B (TMA row strides and bases).
+bool gemv_tc_supported(const void* a, const void* b, int m, int n, int k);
+cudaError_t gemv_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
+                    cudaStream_t stream);
+
 }  // namespace opl

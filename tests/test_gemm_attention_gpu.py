@@ -197,10 +197,14 @@ def test_gemm_f16_deterministic(cuda, stream, m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (2, 1000, 4096), (3, 4104, 333), (8, 2048, 2048),
-                                   (16, 4096, 4096), (16, 8, 7), (5, 8192, 64), (1, 64, 100_000)])
+                                   (16, 4096, 4096), (16, 8, 7), (5, 8192, 64), (1, 64, 100_000),
+                                   (17, 4096, 1024), (32, 2048, 4096), (40, 1000, 520),
+                                   (64, 4096, 4096), (100, 8, 64), (128, 4096, 4096),
+                                   (128, 16384, 512), (1, 128, 8), (7, 136, 72)])
 def test_gemm_f16_skinny(cuda, stream, m, n, k):
-    """Decode-style M <= 16 (split-K SIMT path, fixed-order reduction):
-    FP16 gates and bit-identical repeat runs."""
+    """Skinny M <= 128: swapped-operand tensor-core kernel with a cluster
+    split-K (K % 8 == 0), split-K SIMT kernel otherwise; FP16 gates and
+    bit-identical repeat runs."""
     import torch
 
     rng = np.random.default_rng(m * 7 + n + k)
