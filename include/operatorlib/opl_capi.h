@@ -54,7 +54,7 @@ int opl_reduce_sum_partial_f64(const float* input, double* output, size_t n,
  * memory, fixed memory budgets).  Partial sums go to a fixed file-scope
  * device array of 4096 FP64 slots (32 KiB, held by every GPU that loads the
  * library until exit); a call needing more slots (a device with more than
- * 1024 SMs) returns cudaErrorInvalidValue.  The first call on each device
+ * 4096 SMs) returns cudaErrorInvalidValue.  The first call on each device
  * looks the array up (cudaGetSymbolAddress) and must come before any stream
  * capture.  All calls share the array: calls that overlap on the GPU race;
  * serialise them on one stream.  Same result as opl_reduce_sum_f32. */

@@ -5,16 +5,36 @@
 
 namespace opl {
 
-constexpr int kReduceThreads = 512;
-constexpr int kReduceCtasPerSm = 4;
+constexpr int kReduceThreads = 256;
+// Upper bound on partial-sum CTAs (and so on FP64 partials per call).
+constexpr int kReduceMaxCtas = 4096;
 
 // Per-CTA FP64 partial sums of input[0..n) into partials[blockIdx.x]
 // (kReduceThreads threads; triggers programmatic dependent launch).
 __global__ void reduce_partials_kernel(const float* __restrict__ input, std::size_t n,
                                        double* __restrict__ partials);
 
+// Launches reduce_partials_kernel with `blocks` CTAs on `stream`.
+cudaError_t reduce_partials_launch(const float* input, std::size_t n, double* partials,
+                                   int blocks, cudaStream_t stream);
+
+// Fixed-order sum over a CTA of kReduceThreads threads (warp xor-trees, then
+// the warp totals in warp order); the result is valid in thread 0.
+__device__ __forceinline__ double block_sum_fixed(double v) {
+  __shared__ double warp_totals[kReduceThreads / 32];
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  if (lane == 0) warp_totals[warp] = v;
+  __syncthreads();
+  double total = 0.0;
+  if (threadIdx.x == 0)
+    for (int w = 0; w < kReduceThreads / 32; ++w) total += warp_totals[w];
+  return total;
+}
+
 // Number of partial-sum CTAs used for n elements on the current device
-// (at most sm_count() * kReduceCtasPerSm).
+// (at most kReduceMaxCtas).
 int reduce_grid(std::size_t n);
 
 // Enqueues the partial kernel (blocks CTAs, one FP64 partial each written to

@@ -58,7 +58,7 @@ extern "C" int opl_reduce_sum_f32_noalloc(const float* input, float* output,
                                           size_t n, opl_stream_t stream) {
   if (input == nullptr || output == nullptr || n == 0) return cudaErrorInvalidValue;
   const int blocks = opl::reduce_grid(n);
-  if (blocks > opl::kScratchSlots) return cudaErrorInvalidValue;  // > 1024 SMs
+  if (blocks > opl::kScratchSlots) return cudaErrorInvalidValue;  // > 4096 SMs
   double* scratch = nullptr;
   const cudaError_t error = opl::scratch_address(&scratch);
   if (error != cudaSuccess) return error;

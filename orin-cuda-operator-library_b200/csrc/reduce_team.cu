@@ -52,17 +52,22 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-// One warp: fixed-order sum of this GPU's CTA partials, exchange with the
-// team, fixed-order sum of the team's partials.
-__global__ void __launch_bounds__(32)
+// One CTA: fixed-order sum of this GPU's CTA partials; then its first warp
+// exchanges with the team and sums the team's partials in rank order.
+__global__ void __launch_bounds__(kReduceThreads)
     reduce_team_finalize_kernel(const double* __restrict__ partials, int count,
                                 TeamPeers peers, int rank, int world,
                                 float* __restrict__ output, int* watchdog) {
+  __shared__ double local_total;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int lane = threadIdx.x;
   double v = 0.0;
-  for (int i = lane; i < count; i += 32) v += partials[i];
-  v = warp_sum(v);
+  for (int i = threadIdx.x; i < count; i += kReduceThreads) v += partials[i];
+  v = block_sum_fixed(v);
+  if (threadIdx.x == 0) local_total = v;
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  v = local_total;
 
   TeamBuffer* mine = peers.peer[rank];
   const unsigned long long call = mine->seq + 1;  // same on every rank
@@ -170,12 +175,11 @@ int opl_team_reduce_sum_f32(void* team_ptr, const float* input, float* output, s
   cudaError_t e = cudaMallocAsync(&workspace, blocks * sizeof(double), stream);
   if (e != cudaSuccess) return e;
   double* partials = static_cast<double*>(workspace);
-  reduce_partials_kernel<<<blocks, kReduceThreads, 0, stream>>>(input, n, partials);
-  e = cudaGetLastError();
+  e = reduce_partials_launch(input, n, partials, blocks, stream);
   if (e == cudaSuccess) {
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(1);
-    config.blockDim = dim3(32);
+    config.blockDim = dim3(kReduceThreads);
     config.stream = stream;
     cudaLaunchAttribute attribute[1];
     attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
