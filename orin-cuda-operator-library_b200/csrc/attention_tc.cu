@@ -102,7 +102,8 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap map_q,
                         const __grid_constant__ CUtensorMap map_k,
-                        const __grid_constant__ CUtensorMap map_v, float* __restrict__ out,
+                        const __grid_constant__ CUtensorMap map_v,
+                        const __grid_constant__ CUtensorMap map_o,
                         int heads_total, int seq, int causal, float scale_log2,
                         int tiles_per_cta, int* watchdog) {
   using Cfg = AttnCfg<D>;
@@ -144,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::prefetch_tmap(&map_q);
     tc::prefetch_tmap(&map_k);
     tc::prefetch_tmap(&map_v);
+    tc::prefetch_tmap(&map_o);
   }
   if (warp == 1) tc::tmem_alloc(&bars->tmem_base, kTmemCols);
   tc::tc_fence_before();
@@ -380,20 +382,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_arrive(&bars->p_ready[x]);
     }
     if (ok && tc::mbar_wait_warp(&bars->o_done, 0, abort, watchdog, tc::kWatchdogAttention)) {
+      // Every MMA is done, so Q/K/V shared memory is free: each warp stages
+      // 32 rows x 32 columns of O at a time (128-byte swizzle: thread = row
+      // writes its eight 16-byte pieces at piece ^ (row % 8), conflict-free)
+      // in two 4 KB buffers and writes them with TMA stores (rows past S
+      // are clipped by the tensor map), instead of 32 separate row
+      // segments per store instruction.
       tc::tc_fence_after();
       const float inv = 1.0f / l;
-      float* orow = out + (static_cast<size_t>(bh) * seq + row) * D;
+      uint8_t* stage = smem + Cfg::kQOff + (warp - kSoftmaxWarp0) * 8192;
+      const int y0 = (qt0 + x) * kRowsQ + quarter * 32;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
         tc::tmem_ld32(o_col + c * 32, o);
-        if (row < seq) {
+        uint8_t* buf = stage + (c & 1) * 4096;
+        if (lane == 0) tc::bulk_wait_read<1>();  // the store that used buf is done reading
+        __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            st_stream(reinterpret_cast<float4*>(orow + c * 32 + i),
-                      make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv));
+        for (int k = 0; k < 8; ++k)
+          *reinterpret_cast<float4*>(buf + lane * 128 + ((k ^ (lane & 7)) * 16)) =
+              make_float4(o[4 * k] * inv, o[4 * k + 1] * inv, o[4 * k + 2] * inv,
+                          o[4 * k + 3] * inv);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && y0 < seq) {
+          tc::tma_store_3d(&map_o, buf, c * 32, y0, bh);
+          tc::bulk_commit();
         }
       }
+      if (lane == 0) tc::bulk_wait_all();
     }
   }
 
@@ -408,7 +426,7 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
                                 float* out, int heads_total, int seq, bool causal,
                                 cudaStream_t stream) {
   using Cfg = AttnCfg<D>;
-  CUtensorMap maps[3];
+  CUtensorMap maps[4];
   const __half* ptrs[3] = {q, k, v};
   const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(seq),
                             static_cast<uint64_t>(heads_total)};
@@ -418,6 +436,14 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
   for (int i = 0; i < 3; ++i) {
     const cudaError_t e = encode_tmap(&maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ptrs[i],
                                       dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e != cudaSuccess) return e;
+  }
+  {  // O: FP32 [B*H, S, D], 32 x 32 store boxes
+    const uint64_t o_strides[2] = {static_cast<uint64_t>(D) * 4,
+                                   static_cast<uint64_t>(D) * 4 * seq};
+    const uint32_t o_box[3] = {32, 32, 1};
+    const cudaError_t e = encode_tmap(&maps[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, dims,
+                                      o_strides, o_box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
   }
   cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<D>,
@@ -434,7 +460,7 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
   attention_tc_kernel<D><<<static_cast<unsigned>(ctas), kThreads, Cfg::kSmem, stream>>>(
-      maps[0], maps[1], maps[2], out, heads_total, seq, causal ? 1 : 0, scale_log2,
+      maps[0], maps[1], maps[2], maps[3], heads_total, seq, causal ? 1 : 0, scale_log2,
       tiles_per_cta, watchdog_word());
   return cudaGetLastError();
 }
