@@ -2,9 +2,13 @@
 // softmax state and FP32 output (reference src/attention.cu:222-360 and
 // :486-507 -- there a 16x16 WMMA kernel with QK^T on one warp).
 //
-// One CTA = one (batch*head, pair of 128-query tiles A and B) -- or a single
-// tile A when pairs would leave SMs idle; causal grids start with the
-// longest (bottom) pairs.  320 threads:
+// One CTA = one (batch*head, pair of 128-query tiles A and B); causal grids
+// start with the longest (bottom) pairs.  When pairs would leave SMs idle, a
+// CTA takes one query tile split over the key axis instead ("split mode"):
+// "tile" A handles the even key blocks and "tile" B the odd ones of the same
+// queries (B reads Q_A), each with its own running max, row sum and O
+// accumulator, merged in a fixed order at the end -- so both softmax
+// warpgroups and the tensor-pipe ping-pong stay busy.  320 threads:
 //   warp 0     TMA producer: Q_A, Q_B once; K_j and V_j (128 keys each)
 //              into two 2-slot rings with separate barriers, all 128-byte
 //              swizzled 64-column boxes of a 3-D [B*H, S, D] tensor map
@@ -54,7 +58,8 @@ struct AttnCfg {
   static constexpr int kKOff = 2 * kTileBytes;       // K slots 0, 1
   static constexpr int kVOff = 4 * kTileBytes;       // V slots 0, 1
   static constexpr int kBarOff = 6 * kTileBytes;
-  static constexpr size_t kSmem = kBarOff + 256 + 1024;
+  static constexpr int kXchgOff = kBarOff + 256;  // split mode: (m, l) of both halves
+  static constexpr size_t kSmem = kXchgOff + 2048 + 1024;
   static constexpr uint32_t kIdescQK = tc::idesc_f16_f32(kRowsQ, kKeys, false, false);
   static constexpr uint32_t kIdescPV = tc::idesc_f16_f32(kRowsQ, D, false, true);
   static constexpr uint32_t kColO0 = 2 * kKeys;  // O_A; O_B follows at +D
@@ -69,7 +74,6 @@ struct AttnBars {
   uint64_t s_full[2];   // per tile X
   uint64_t p_ready[2];  // per tile X
   uint64_t o_done;
-  uint64_t pv_done;  // single-tile mode: PV(j) complete
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -87,6 +91,11 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Named barrier 1 over `count` threads.
+__device__ __forceinline__ void bar_sync_named(int count) {
+  asm volatile("bar.sync 1, %0;" ::"r"(count) : "memory");
 }
 
 __device__ __forceinline__ float pack_half2_bits(float lo, float hi) {
@@ -120,12 +129,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = blockIdx.x % heads_total;
   const int pair = pairs - 1 - static_cast<int>(blockIdx.x / heads_total);
   const int qt0 = tiles_per_cta * pair;
-  const bool valid_b = tiles_per_cta == 2 && qt0 + 1 < q_tiles;
+  const bool split = tiles_per_cta == 1;
+  const bool valid_b = tiles_per_cta == 2 && qt0 + 1 < q_tiles;  // a second Q tile
   const int kv_all = (seq + kKeys - 1) / kKeys;
+  // n_tiles[x]: key blocks tile x processes; n_load: key blocks loaded.
   int n_tiles[2];
-  n_tiles[0] = causal ? min(kv_all, qt0 + 1) : kv_all;
-  n_tiles[1] = valid_b ? (causal ? min(kv_all, qt0 + 2) : kv_all) : 0;
-  const int n_max = max(n_tiles[0], n_tiles[1]);
+  int n_load;
+  if (split) {
+    n_load = causal ? min(kv_all, qt0 + 1) : kv_all;
+    n_tiles[0] = (n_load + 1) / 2;  // blocks 0, 2, 4, ...
+    n_tiles[1] = n_load / 2;        // blocks 1, 3, 5, ...
+  } else {
+    n_tiles[0] = causal ? min(kv_all, qt0 + 1) : kv_all;
+    n_tiles[1] = valid_b ? (causal ? min(kv_all, qt0 + 2) : kv_all) : 0;
+    n_load = max(n_tiles[0], n_tiles[1]);
+  }
 
   if (threadIdx.x == 0) {
     tc::mbar_init(&bars->q_full, 1);
@@ -138,7 +156,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::mbar_init(&bars->p_ready[i], 128);
     }
     tc::mbar_init(&bars->o_done, 1);
-    tc::mbar_init(&bars->pv_done, 1);
     tc::mbar_init(&bars->drain, 1);
     bars->abort = 0;
     tc::fence_barrier_init();
@@ -152,6 +169,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // Launched with programmatic dependent launch: the set-up above overlaps
+  // the previous kernel on the stream; global memory is touched only after
+  // it has completed.  The next kernel may start its own set-up at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0 && lane == 0) {
     // ---------------------------------------------------------- producer
@@ -162,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int b = 0; b < Cfg::kBoxes; ++b)
         tc::tma_load_3d(smem + Cfg::kQOff + x * Cfg::kTileBytes + b * Cfg::kBoxBytes, &map_q,
                         b * 64, (qt0 + x) * kRowsQ, bh, &bars->q_full);
-    for (int j = 0; j < n_max && !*abort; ++j) {
+    for (int j = 0; j < n_load && !*abort; ++j) {
       const int st = j & 1;
       const uint32_t ph = (j >> 1) & 1;
       if (!tc::mbar_wait(&bars->k_empty[st], ph ^ 1, abort, watchdog, tc::kWatchdogAttention))
@@ -211,9 +233,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       issued_any = true;
     };
     auto qk = [&](int x, int j) { qk_into(x, x, j); };
+    // In split mode tile x handles key block b = 2 j + x, which sits in
+    // ring slot b & 1 == x with phase (b >> 1) & 1 == j & 1.
     // O_x += P (FP16 pairs in the first 64 columns of S block `buf`; 8
     // packed columns per 16 keys) * V_j.
-    auto pv_from = [&](int buf, int x, int j) {
+    auto pv_from = [&](int buf, int x, int j, bool first) {
       const uint32_t v_addr = tc::smem_u32(smem + Cfg::kVOff + (j & 1) * Cfg::kTileBytes);
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk)
@@ -221,35 +245,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         // apart); a 16-key step is two 8-row groups (2 KB).
         tc::umma_f16_tmem_a(tmem + Cfg::kColO0 + x * D, tmem + buf * kKeys + kk * 8,
                             tc::smem_desc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024),
-                            Cfg::kIdescPV, (j | kk) != 0);
+                            Cfg::kIdescPV, !(first && kk == 0));
       issued_any = true;
     };
-    auto pv = [&](int x, int j) { pv_from(x, x, j); };
+    auto pv = [&](int x, int j) { pv_from(x, x, j, j == 0); };
     auto wait = [&](uint64_t* bar, uint32_t parity) {
       const bool ok = tc::mbar_wait(bar, parity, abort, watchdog, tc::kWatchdogAttention);
       if (ok) tc::tc_fence_after();
       return ok;
     };
     bool ok = wait(&bars->q_full, 0) && wait(&bars->k_full[0], 0);
-    if (tiles_per_cta == 1) {
-      // One tile: S alternates between the two S column blocks, so QK(j+1)
-      // runs while the softmax works on S(j).
+    if (split) {
+      // Per tile x: PV_x(j), then QK_x(j+1) -- S_x(j+1) is committed after
+      // PV_x(j), so a softmax warp that sees it finds O_x stable.
       if (ok) {
-        qk(0, 0);  // into block 0
+        qk_into(0, 0, 0);
         tc::umma_commit(&bars->k_empty[0]);
-      }
-      const int n = n_tiles[0];
-      for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n) {
-          if (!wait(&bars->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) break;
-          qk_into((j + 1) & 1, 0, j + 1);
-          tc::umma_commit(&bars->k_empty[(j + 1) & 1]);
+        if (n_tiles[1] > 0) {
+          ok = wait(&bars->k_full[1], 0);
+          if (ok) {
+            qk_into(1, 0, 1);
+            tc::umma_commit(&bars->k_empty[1]);
+          }
         }
-        if (!wait(&bars->v_full[j & 1], (j >> 1) & 1)) break;
-        if (!wait(&bars->p_ready[0], j & 1)) break;
-        pv_from(j & 1, 0, j);
-        tc::umma_commit(&bars->pv_done);
-        tc::umma_commit(&bars->v_empty[j & 1]);
+      }
+      for (int j = 0; ok && j < n_tiles[0]; ++j) {
+        for (int x = 0; ok && x < 2; ++x) {
+          if (j >= n_tiles[x]) continue;
+          const int b = 2 * j + x;
+          ok = wait(&bars->v_full[x], j & 1) && wait(&bars->p_ready[x], j & 1);
+          if (!ok) break;
+          pv_from(x, x, b, j == 0);
+          tc::umma_commit(&bars->v_empty[x]);
+          if (j + 1 < n_tiles[x]) {
+            ok = wait(&bars->k_full[x], (j + 1) & 1);
+            if (!ok) break;
+            qk_into(x, 0, b + 2);
+            tc::umma_commit(&bars->k_empty[x]);
+          }
+        }
       }
     } else {
       if (ok) {
@@ -257,7 +291,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n_tiles[1] > 0) qk(1, 0);
         tc::umma_commit(&bars->k_empty[0]);
       }
-      for (int j = 0; ok && j < n_max; ++j) {
+      for (int j = 0; ok && j < n_load; ++j) {
         const bool do_a = j < n_tiles[0], do_b = j < n_tiles[1];
         const bool next_a = j + 1 < n_tiles[0], next_b = j + 1 < n_tiles[1];
         if (!wait(&bars->v_full[j & 1], (j >> 1) & 1)) break;
@@ -291,9 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int x = (warp - kSoftmaxWarp0) >> 2;  // tile A or B
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // row in tile == TMEM lane
-    const int row = (qt0 + x) * kRowsQ + r;
+    const int row = (qt0 + (split ? 0 : x)) * kRowsQ + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const bool single = tiles_per_cta == 1;
     const uint32_t o_col = tmem + lane_off + Cfg::kColO0 + x * D;
     const int limit = causal ? min(seq - 1, row) : seq - 1;  // last visible key
     const int n = n_tiles[x];
@@ -301,11 +334,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l = 0.0f;
     bool ok = n > 0;
     for (int j = 0; ok && j < n; ++j) {
-      // S block: the tile's own in pair mode, alternating in single mode.
-      const int buf = single ? (j & 1) : x;
-      const uint32_t s_col = tmem + lane_off + buf * kKeys;
-      if (!tc::mbar_wait_warp(&bars->s_full[buf], single ? (j >> 1) & 1 : j & 1, abort,
-                              watchdog, tc::kWatchdogAttention)) {
+      const uint32_t s_col = tmem + lane_off + x * kKeys;
+      if (!tc::mbar_wait_warp(&bars->s_full[x], j & 1, abort, watchdog,
+                              tc::kWatchdogAttention)) {
         ok = false;
         break;
       }
@@ -320,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < kKeys; ++i) s[i] = __uint_as_float(raw[i]);
       }
-      const int key0 = j * kKeys;
+      const int key0 = (split ? 2 * j + x : j) * kKeys;
       if (key0 + kKeys - 1 > limit) {  // edge tile: mask keys past the limit
 #pragma unroll
         for (int i = 0; i < kKeys; ++i)
@@ -362,13 +393,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O_x is stable here (S_x(j) was committed after PV_x(j-1), and
       // PV_x(j) waits for p_ready); rescaled after P is out of registers.
       if (j > 0 && __any_sync(kFullMask, alpha != 1.0f)) {
-        // Single mode: S(j) was issued before PV(j-1), so wait for it here.
-        if (single && !tc::mbar_wait_warp(&bars->pv_done, (j - 1) & 1, abort, watchdog,
-                                          tc::kWatchdogAttention)) {
-          ok = false;
-          break;
-        }
-        tc::tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           float o[32];
@@ -381,7 +405,62 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::tc_fence_before();
       tc::mbar_arrive(&bars->p_ready[x]);
     }
-    if (ok && tc::mbar_wait_warp(&bars->o_done, 0, abort, watchdog, tc::kWatchdogAttention)) {
+    if (split) {
+      // Merge the halves: m = max(m_A, m_B), O = (O_A 2^(m_A - m) +
+      // O_B 2^(m_B - m)) / (l_A 2^(m_A - m) + l_B 2^(m_B - m)).  Every
+      // softmax thread passes the named barrier exactly once.  Half x then
+      // writes O columns [x D/2, (x + 1) D/2) through TMA stores.
+      float* xch = reinterpret_cast<float*>(smem + Cfg::kXchgOff);  // [x][m, l][row]
+      xch[(2 * x) * kRowsQ + r] = m_used;
+      xch[(2 * x + 1) * kRowsQ + r] = l;
+      const bool done = (ok || n == 0) && tc::mbar_wait_warp(&bars->o_done, 0, abort, watchdog,
+                                                            tc::kWatchdogAttention);
+      bar_sync_named(256);
+      if (done) {
+        tc::tc_fence_after();
+        const bool has_b = n_tiles[1] > 0;
+        const float ma = xch[r], la = xch[kRowsQ + r];
+        const float mb = has_b ? xch[2 * kRowsQ + r] : -INFINITY;
+        const float lb = has_b ? xch[3 * kRowsQ + r] : 0.0f;
+        const float m = fmaxf(ma, mb);
+        const float ca = exp2f(ma - m);
+        const float cb = mb == -INFINITY ? 0.0f : exp2f(mb - m);
+        const float inv = 1.0f / (la * ca + lb * cb);
+        const float wa = ca * inv, wb = cb * inv;
+        const uint32_t oa_col = tmem + lane_off + Cfg::kColO0;
+        uint8_t* stage = smem + Cfg::kQOff + (warp - kSoftmaxWarp0) * 8192;
+        const int y0 = qt0 * kRowsQ + quarter * 32;
+#pragma unroll 1
+        for (int c = 0; c < D / 64; ++c) {
+          const int col = x * (D / 2) + c * 32;
+          float o[32];
+          tc::tmem_ld32(oa_col + col, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= wa;
+          if (has_b) {
+            float ob[32];
+            tc::tmem_ld32(oa_col + D + col, ob);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = fmaf(ob[i], wb, o[i]);
+          }
+          uint8_t* buf = stage + (c & 1) * 4096;
+          if (lane == 0) tc::bulk_wait_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            *reinterpret_cast<float4*>(buf + lane * 128 + ((k ^ (lane & 7)) * 16)) =
+                make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+          tc::fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && y0 < seq) {
+            tc::tma_store_3d(&map_o, buf, col, y0, bh);
+            tc::bulk_commit();
+          }
+        }
+        if (lane == 0) tc::bulk_wait_read<0>();  // smem reads done; the grid end publishes the writes
+      }
+    } else if (ok &&
+               tc::mbar_wait_warp(&bars->o_done, 0, abort, watchdog, tc::kWatchdogAttention)) {
       // Every MMA is done, so Q/K/V shared memory is free: each warp stages
       // 32 rows x 32 columns of O at a time (128-byte swizzle: thread = row
       // writes its eight 16-byte pieces at piece ^ (row % 8), conflict-free)
@@ -411,7 +490,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::bulk_commit();
         }
       }
-      if (lane == 0) tc::bulk_wait_all();
+      if (lane == 0) tc::bulk_wait_read<0>();  // smem reads done; the grid end publishes the writes
     }
   }
 
@@ -459,10 +538,19 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
       static_cast<long long>(heads_total) * ((q_tiles + tiles_per_cta - 1) / tiles_per_cta);
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
   const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
-  attention_tc_kernel<D><<<static_cast<unsigned>(ctas), kThreads, Cfg::kSmem, stream>>>(
-      maps[0], maps[1], maps[2], maps[3], heads_total, seq, causal ? 1 : 0, scale_log2,
-      tiles_per_cta, watchdog_word());
-  return cudaGetLastError();
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(ctas));
+  config.blockDim = dim3(kThreads);
+  config.dynamicSmemBytes = Cfg::kSmem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, attention_tc_kernel<D>, maps[0], maps[1], maps[2], maps[3],
+                            heads_total, seq, causal ? 1 : 0, scale_log2, tiles_per_cta,
+                            watchdog_word());
 }
 
 }  // namespace
