@@ -128,6 +128,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // Programmatic dependent launch: the set-up above overlaps the previous
+  // kernel on the stream; global memory is touched only after it completed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -273,13 +277,15 @@ cudaError_t launch_gemv_tc(const __half* a, const __half* b, float* c, int m, in
   config.blockDim = dim3(kThreads);
   config.dynamicSmemBytes = Cfg::kSmem;
   config.stream = stream;
-  cudaLaunchAttribute attribute[1];
+  cudaLaunchAttribute attribute[2];
   attribute[0].id = cudaLaunchAttributeClusterDimension;
   attribute[0].val.clusterDim.x = static_cast<unsigned>(cs);
   attribute[0].val.clusterDim.y = 1;
   attribute[0].val.clusterDim.z = 1;
+  attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[1].val.programmaticStreamSerializationAllowed = 1;
   config.attrs = attribute;
-  config.numAttrs = 1;
+  config.numAttrs = 2;
   return cudaLaunchKernelEx(&config, gemv_tc_kernel<MP>, map_b, map_a, c, m, n, n, k_blocks,
                             kb_per, watchdog_word());
 }
