@@ -31,4 +31,11 @@ bool gemv_tc_supported(const void* a, const void* b, int m, int n, int k);
 cudaError_t gemv_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
                     cudaStream_t stream);
 
+// Skinny-N FP16 product on the same kernel: C[i][j] (row stride ldc) =
+// sum_k A[i][k] * bt[j][k] for i < m, j < ns <= 128; A row stride lda and
+// bt ([ns][k], row stride ldbt) -- strides multiples of 8 halves, 16-byte
+// aligned bases.
+cudaError_t gemm_small_n_tc(const __half* a, int lda, const __half* bt, int ldbt, float* c,
+                            int ldc, int m, int ns, int k, cudaStream_t stream);
+
 }  // namespace opl

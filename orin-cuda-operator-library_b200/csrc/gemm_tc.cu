@@ -393,38 +393,70 @@ cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, in
   return cudaGetLastError();
 }
 
+// The n_tail columns [n_main, n_main + n_tail) of B (row stride ldb, k rows)
+// as a K-major strip bt[j][kk] (row stride kp; zero for kk >= k).
+__global__ void __launch_bounds__(256)
+    tail_columns_kernel(const __half* __restrict__ b, int k, int ldb, int n_main, int n_tail,
+                        __half* __restrict__ bt, int kp) {
+  const int kk = blockIdx.x * 256 + threadIdx.x;
+  if (kk >= kp) return;
+  for (int j = 0; j < n_tail; ++j)
+    bt[static_cast<size_t>(j) * kp + kk] =
+        kk < k ? b[static_cast<size_t>(kk) * ldb + n_main + j] : __float2half(0.0f);
+}
+
 }  // namespace
 
 // Tensor-core GEMM for any shape: strides that TMA cannot address (rows not
 // a multiple of 16 bytes, or unaligned bases) go through zero-padded copies
-// in a stream-ordered workspace.
+// in a stream-ordered workspace.  When N ends in a narrow remainder (at most
+// 64 columns past a multiple of the 256-wide tile), the 256-wide kernel
+// covers the first n_main columns and the remainder runs as a skinny-N
+// product (gemm_small_n_tc) -- instead of one extra, almost empty tile per
+// 128 rows (4095 x 4097 x 4093: 544 tiles and a fourth wave vs 512 tiles).
 cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
                         cudaStream_t stream) {
   const bool a_ok = (k % 8 == 0) && aligned16(a);
   const bool b_ok = (n % 8 == 0) && (k % 8 == 0) && aligned16(b);
-  if (a_ok && b_ok) return launch_gemm_tc(a, b, c, m, n, k, k, n, n, stream);
+  const int n_tail = n % kBN;
+  const bool split_n = n > kBN && n_tail != 0 && n_tail <= 64 && m > 128;
+  if (a_ok && b_ok && !split_n) return launch_gemm_tc(a, b, c, m, n, k, k, n, n, stream);
 
   const int kp = (k + 7) & ~7;
-  const int np = b_ok ? n : ((n + 7) & ~7);
+  const int n_main = split_n ? n - n_tail : n;
+  // B as the big kernel reads it: the caller's (b_ok) or a padded copy of
+  // its first n_main columns (n_main rounded up to 8 without a split).
+  const int ldb_copy = split_n ? n_main : ((n + 7) & ~7);
   const size_t a_elems = a_ok ? 0 : static_cast<size_t>(m) * kp;
-  const size_t b_elems = b_ok ? 0 : static_cast<size_t>(kp) * np;
+  const size_t b_elems = b_ok ? 0 : static_cast<size_t>(kp) * ldb_copy;
+  const size_t t_elems = split_n ? static_cast<size_t>(n_tail) * kp : 0;
   const size_t a_bytes = (a_elems * 2 + 255) & ~size_t(255);
+  const size_t b_bytes = (b_elems * 2 + 255) & ~size_t(255);
   void* ws = nullptr;
-  cudaError_t e = cudaMallocAsync(&ws, a_bytes + b_elems * 2 + 16, stream);
+  cudaError_t e = cudaMallocAsync(&ws, a_bytes + b_bytes + t_elems * 2 + 16, stream);
   if (e != cudaSuccess) return e;
-  __half* a_use = const_cast<__half*>(a);
-  __half* b_use = const_cast<__half*>(b);
+  uint8_t* wsb = static_cast<uint8_t*>(ws);
+  const __half* a_use = a;
+  const __half* b_use = b;
   if (!a_ok) {
-    a_use = static_cast<__half*>(ws);
-    pad_half_kernel<<<m < 65535 ? m : 65535, 256, 0, stream>>>(a, m, k, a_use, m, kp);
+    __half* dst = reinterpret_cast<__half*>(wsb);
+    pad_half_kernel<<<m < 65535 ? m : 65535, 256, 0, stream>>>(a, m, k, dst, m, kp);
+    a_use = dst;
   }
   if (!b_ok) {
-    b_use = reinterpret_cast<__half*>(static_cast<uint8_t*>(ws) + a_bytes);
-    pad_half_kernel<<<kp < 65535 ? kp : 65535, 256, 0, stream>>>(b, k, n, b_use, kp, np);
+    __half* dst = reinterpret_cast<__half*>(wsb + a_bytes);
+    pad_half_kernel<<<kp < 65535 ? kp : 65535, 256, 0, stream>>>(b, k, n, dst, kp, ldb_copy);
+    b_use = dst;
   }
+  __half* bt = reinterpret_cast<__half*>(wsb + a_bytes + b_bytes);
+  if (split_n)
+    tail_columns_kernel<<<(kp + 255) / 256, 256, 0, stream>>>(b, k, n, n_main, n_tail, bt, kp);
   e = cudaGetLastError();
-  if (e == cudaSuccess)
-    e = launch_gemm_tc(a_use, b_use, c, m, n, kp, a_ok ? k : kp, b_ok ? n : np, n, stream);
+  const int lda = a_ok ? k : kp;
+  const int ldb = b_ok ? n : ldb_copy;
+  if (e == cudaSuccess) e = launch_gemm_tc(a_use, b_use, c, m, n_main, kp, lda, ldb, n, stream);
+  if (e == cudaSuccess && split_n)
+    e = gemm_small_n_tc(a_use, lda, bt, kp, c + n_main, n, m, n_tail, kp, stream);
   const cudaError_t f = cudaFreeAsync(ws, stream);
   return e != cudaSuccess ? e : f;
 }

@@ -21,6 +21,12 @@
 // through distributed shared memory and stores them.  One launch, no
 // workspace, and a fixed summation order: results are deterministic.
 //
+// The same kernel serves skinny-N products (kSmallN): C[M, n] = A[M,K] B[K,n]
+// for n <= 128 (the tail columns of a GEMM whose N is not a multiple of the
+// big kernel's 256-wide tiles), with A as the big K-major operand (one
+// 128 x 64 box per K block) and the n columns of B, transposed into a
+// K-major [Np, K] strip, as the small one.
+//
 // No cluster multicast is used (each CTA loads its own tiles).  Every
 // mbarrier wait is bounded; a wait that gives up sets the watchdog word,
 // the CTA drains its outstanding copies and MMAs and still reaches both
@@ -42,13 +48,13 @@ constexpr int kMaxCluster = 8;
 constexpr size_t kRingBudget = 200 * 1024;
 constexpr int kWatchdogGemv = 0x6e05;
 
-template <int MP>
+template <int MP, bool kSmallN>
 struct GemvCfg {
   static constexpr int kABytes = MP * kBK * 2;  // Mp rows x 128 B
   static constexpr int kStageBytes = kBtBytes + kABytes;
   static constexpr int kStages = static_cast<int>(kRingBudget / kStageBytes);
   static constexpr uint32_t kTmemCols = MP < 32 ? 32 : MP;
-  static constexpr uint32_t kIdesc = tc::idesc_f16_f32(kTile, MP, true, false);
+  static constexpr uint32_t kIdesc = tc::idesc_f16_f32(kTile, MP, !kSmallN, false);
   static constexpr int kRedBytes = MP * kTile * 4;  // partial tile, aliases the ring
   static_assert(kRedBytes <= kStages * kStageBytes, "partial tile must fit in the ring");
   static constexpr size_t kSmem = static_cast<size_t>(kStages) * kStageBytes + 1024 + 512;
@@ -88,12 +94,14 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
   return v;
 }
 
-template <int MP>
+// map_b: the big operand (B, or A when kSmallN); map_a: the small one.  n is
+// the big extent (columns of C, or rows when kSmallN), m the small one.
+template <int MP, bool kSmallN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_a, float* __restrict__ c, int m,
                    int n, int ldc, int k_blocks, int kb_per, int* watchdog) {
-  using Cfg = GemvCfg<MP>;
+  using Cfg = GemvCfg<MP, kSmallN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -143,8 +151,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       uint8_t* sb = smem + stage * Cfg::kStageBytes;
       tc::mbar_expect_tx(&bars->full[stage], Cfg::kStageBytes);
-      tc::tma_load_2d(sb, &map_b, n0, kb * kBK, &bars->full[stage]);
-      tc::tma_load_2d(sb + kBoxBytes, &map_b, n0 + 64, kb * kBK, &bars->full[stage]);
+      if (kSmallN) {
+        tc::tma_load_2d(sb, &map_b, kb * kBK, n0, &bars->full[stage]);  // 128 rows x 64 K
+      } else {
+        tc::tma_load_2d(sb, &map_b, n0, kb * kBK, &bars->full[stage]);
+        tc::tma_load_2d(sb + kBoxBytes, &map_b, n0 + 64, kb * kBK, &bars->full[stage]);
+      }
       tc::tma_load_2d(sb + kBtBytes, &map_a, kb * kBK, 0, &bars->full[stage]);
       issued_mask |= 1u << stage;
       issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -175,7 +187,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // B^T: MN-major, two 64-column boxes 8 KB apart, a 16-deep K step is
         // two 8-row groups (2 KB).  A^T: K-major 128-byte rows, a K step is
         // 32 B inside the swizzle atom.
-        const uint64_t bt_desc = tc::smem_desc_sw128(bt + kk * 2048, kBoxBytes, 1024);
+        // (kSmallN: the big operand is K-major like A^T.)
+        const uint64_t bt_desc = kSmallN ? tc::smem_desc_sw128(bt + kk * 32, 16, 1024)
+                                         : tc::smem_desc_sw128(bt + kk * 2048, kBoxBytes, 1024);
         const uint64_t at_desc = tc::smem_desc_sw128(at + kk * 32, 16, 1024);
         tc::umma_f16(tmem, bt_desc, at_desc, Cfg::kIdesc, (kb != kb0) || (kk != 0));
       }
@@ -211,7 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (cluster_n == 1) {
 #pragma unroll
       for (int r = 0; r < 32; ++r)
-        if (col < n && r < rows && c0 + r < m) c[static_cast<size_t>(c0 + r) * ldc + col] = v[r];
+        if (col < n && r < rows && c0 + r < m)
+          c[kSmallN ? static_cast<size_t>(col) * ldc + c0 + r
+                    : static_cast<size_t>(c0 + r) * ldc + col] = v[r];
     } else {
 #pragma unroll
       for (int r = 0; r < 32; ++r)
@@ -225,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int r = static_cast<int>(rank); r < m; r += static_cast<int>(cluster_n)) {
         float s = 0.0f;
         for (uint32_t p = 0; p < cluster_n; ++p) s += ld_cluster_f32(red + r * kTile + t, p);
-        c[static_cast<size_t>(r) * ldc + col] = s;
+        c[kSmallN ? static_cast<size_t>(col) * ldc + r : static_cast<size_t>(r) * ldc + col] = s;
       }
     cluster_sync_all();  // peers keep their shared memory until all reads are done
   }
@@ -236,34 +252,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) tc::tmem_dealloc(tmem, Cfg::kTmemCols);
 }
 
-template <int MP>
-cudaError_t launch_gemv_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
-                           cudaStream_t stream) {
-  using Cfg = GemvCfg<MP>;
+// Encodes the maps and launches.  Skinny-M: big = B [k][n] (row stride ldb),
+// small = A [m][k].  Skinny-N: big = A [m_big][k] (row stride lda), small =
+// the K-major strip [Np][k] (row stride ld_small); `n` is then m_big and `m`
+// the number of tail columns.
+template <int MP, bool kSmallN>
+cudaError_t launch_gemv_tc(const __half* big, int ld_big, const __half* small, int ld_small,
+                           float* c, int ldc, int m, int n, int k, cudaStream_t stream) {
+  using Cfg = GemvCfg<MP, kSmallN>;
   CUtensorMap map_b, map_a;
   {
-    const uint64_t dims[2] = {static_cast<uint64_t>(n), static_cast<uint64_t>(k)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(n) * 2};
-    const uint32_t box[2] = {64, kBK};
-    cudaError_t e = encode_tmap(&map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, dims, strides,
+    const uint64_t dims[2] = {kSmallN ? static_cast<uint64_t>(k) : static_cast<uint64_t>(n),
+                              kSmallN ? static_cast<uint64_t>(n) : static_cast<uint64_t>(k)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ld_big) * 2};
+    const uint32_t box[2] = {64, kSmallN ? static_cast<uint32_t>(kTile) : kBK};
+    cudaError_t e = encode_tmap(&map_b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, big, dims, strides,
                                 box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
   }
   {
+    // Rows past m (the small extent) read as zero.
     const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(k) * 2};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ld_small) * 2};
     const uint32_t box[2] = {kBK, MP};
-    cudaError_t e = encode_tmap(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, dims, strides,
-                                box, CU_TENSOR_MAP_SWIZZLE_128B);
+    cudaError_t e = encode_tmap(&map_a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, small, dims,
+                                strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
   }
-  cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<MP>,
+  cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<MP, kSmallN>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(Cfg::kSmem));
   if (e != cudaSuccess) return e;
 
-  // Column tiles x K splits: as many splits (one per cluster CTA, at most 8)
-  // as keep tiles * splits within the SM count, every split non-empty.
+  // Tiles of 128 along the big extent x K splits: as many splits (one per
+  // cluster CTA, at most 8) as keep tiles * splits within the SM count,
+  // every split non-empty.
   const int tiles = (n + kTile - 1) / kTile;
   const int k_blocks = (k + kBK - 1) / kBK;
   int cs = sm_count() / tiles;
@@ -286,8 +309,8 @@ cudaError_t launch_gemv_tc(const __half* a, const __half* b, float* c, int m, in
   attribute[1].val.programmaticStreamSerializationAllowed = 1;
   config.attrs = attribute;
   config.numAttrs = 2;
-  return cudaLaunchKernelEx(&config, gemv_tc_kernel<MP>, map_b, map_a, c, m, n, n, k_blocks,
-                            kb_per, watchdog_word());
+  return cudaLaunchKernelEx(&config, gemv_tc_kernel<MP, kSmallN>, map_b, map_a, c, m, n, ldc,
+                            k_blocks, kb_per, watchdog_word());
 }
 
 }  // namespace
@@ -298,10 +321,18 @@ bool gemv_tc_supported(const void* a, const void* b, int m, int n, int k) {
 
 cudaError_t gemv_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
                     cudaStream_t stream) {
-  if (m <= 16) return launch_gemv_tc<16>(a, b, c, m, n, k, stream);
-  if (m <= 32) return launch_gemv_tc<32>(a, b, c, m, n, k, stream);
-  if (m <= 64) return launch_gemv_tc<64>(a, b, c, m, n, k, stream);
-  return launch_gemv_tc<128>(a, b, c, m, n, k, stream);
+  if (m <= 16) return launch_gemv_tc<16, false>(b, n, a, k, c, n, m, n, k, stream);
+  if (m <= 32) return launch_gemv_tc<32, false>(b, n, a, k, c, n, m, n, k, stream);
+  if (m <= 64) return launch_gemv_tc<64, false>(b, n, a, k, c, n, m, n, k, stream);
+  return launch_gemv_tc<128, false>(b, n, a, k, c, n, m, n, k, stream);
+}
+
+cudaError_t gemm_small_n_tc(const __half* a, int lda, const __half* bt, int ldbt, float* c,
+                            int ldc, int m, int ns, int k, cudaStream_t stream) {
+  if (ns <= 16) return launch_gemv_tc<16, true>(a, lda, bt, ldbt, c, ldc, ns, m, k, stream);
+  if (ns <= 32) return launch_gemv_tc<32, true>(a, lda, bt, ldbt, c, ldc, ns, m, k, stream);
+  if (ns <= 64) return launch_gemv_tc<64, true>(a, lda, bt, ldbt, c, ldc, ns, m, k, stream);
+  return launch_gemv_tc<128, true>(a, lda, bt, ldbt, c, ldc, ns, m, k, stream);
 }
 
 }  // namespace opl

@@ -45,7 +45,10 @@ def check_f16(got, want):
 GEMM_F16 = [(128, 128, 32), (16, 128, 32), (32, 32, 32), (37, 65, 71),  # ref tests
             (17, 19, 23), (1, 256, 64), (1, 1, 1), (128, 256, 64), (256, 512, 1024),
             (1000, 1000, 1000), (512, 4096, 4096), (4095, 4097, 4093),
-            (4096, 4096, 4096), (300, 520, 136), (129, 257, 72)]
+            (4096, 4096, 4096), (300, 520, 136), (129, 257, 72),
+            # narrow N remainders: 256-wide kernel + skinny-N tail product
+            (1000, 4104, 512), (257, 300, 64), (200, 320, 96), (129, 513, 1000),
+            (640, 769, 333)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_F16)
