@@ -276,14 +276,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(256)
     zero_tail_tiles_kernel(float* __restrict__ c, int m, int n, int k, int ldc,
                            int grid_ctas) {
+  // blockIdx.x: tail tile; blockIdx.y: its 8-row slice (16 per tile).
   TileGrid grid;
   grid.init(m, n, k, grid_ctas, true);
   int mb, nb;
   grid.coords(grid.tiles_full + blockIdx.x, mb, nb);
   const int col = nb * kBN + threadIdx.x;  // kBN == blockDim.x
   if (col >= n) return;
-  const int row_end = min(m, (mb + 1) * kBM);
-  for (int row = mb * kBM; row < row_end; ++row) c[static_cast<size_t>(row) * ldc + col] = 0.0f;
+  const int row0 = mb * kBM + blockIdx.y * (kBM / 16);
+  const int row_end = min(m, row0 + kBM / 16);
+#pragma unroll 8
+  for (int row = row0; row < row_end; ++row) c[static_cast<size_t>(row) * ldc + col] = 0.0f;
 }
 
 // Eight halves starting at half `o` (0..7) of the 16 halves in w[0..7]
@@ -314,10 +317,15 @@ __device__ __forceinline__ uint4 halves_at(const uint32_t (&w)[8], int o) {
 // any row stride) into a prow x pcol buffer (pcol a multiple of 8, so every row
 // starts 16-byte aligned for TMA).  Each output group of 8 halves is built
 // from the two aligned 16-byte source words that cover it and a byte shift
-// that is fixed per row, so all loads and stores are 128-bit.
+// that is fixed per row, so all loads and stores are 128-bit.  With
+// tail != nullptr it also gathers columns [tail_col0, tail_col0 + n_tail)
+// (n_tail <= blockDim.x) into the K-major strip tail[j][r] (row stride
+// tail_ld; zero for r >= rows).
 __global__ void __launch_bounds__(256)
     pad_half_kernel(const __half* __restrict__ src, int rows, int cols,
-                    __half* __restrict__ dst, int prow, int pcol) {
+                    __half* __restrict__ dst, int prow, int pcol,
+                    __half* __restrict__ tail = nullptr, int tail_col0 = 0, int n_tail = 0,
+                    int tail_ld = 0) {
   const int groups = pcol / 8;
   // Work from the 16-byte-aligned word holding the first element (inside
   // the caller's allocation, whose base is 256-byte aligned).
@@ -349,6 +357,10 @@ __global__ void __launch_bounds__(256)
       }
       drow[g] = out;
     }
+    if (tail != nullptr && static_cast<int>(threadIdx.x) < n_tail)
+      tail[static_cast<size_t>(threadIdx.x) * tail_ld + r] =
+          r < rows ? src[static_cast<size_t>(r) * cols + tail_col0 + threadIdx.x]
+                   : __float2half(0.0f);
   }
 }
 
@@ -384,7 +396,7 @@ cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, in
   const bool split_tail = tiles > grid && tail != 0 && 2 * tail <= grid &&
                           (k + kBK - 1) / kBK >= 8;
   if (split_tail) {
-    zero_tail_tiles_kernel<<<tail, kBN, 0, stream>>>(c, m, n, k, ldc, grid);
+    zero_tail_tiles_kernel<<<dim3(tail, 16), kBN, 0, stream>>>(c, m, n, k, ldc, grid);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -443,14 +455,15 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
     pad_half_kernel<<<m < 65535 ? m : 65535, 256, 0, stream>>>(a, m, k, dst, m, kp);
     a_use = dst;
   }
-  if (!b_ok) {
-    __half* dst = reinterpret_cast<__half*>(wsb + a_bytes);
-    pad_half_kernel<<<kp < 65535 ? kp : 65535, 256, 0, stream>>>(b, k, n, dst, kp, ldb_copy);
-    b_use = dst;
-  }
   __half* bt = reinterpret_cast<__half*>(wsb + a_bytes + b_bytes);
-  if (split_n)
+  if (!b_ok) {  // (with a split, the same pass gathers the tail columns)
+    __half* dst = reinterpret_cast<__half*>(wsb + a_bytes);
+    pad_half_kernel<<<kp < 65535 ? kp : 65535, 256, 0, stream>>>(
+        b, k, n, dst, kp, ldb_copy, split_n ? bt : nullptr, n_main, n_tail, kp);
+    b_use = dst;
+  } else if (split_n) {
     tail_columns_kernel<<<(kp + 255) / 256, 256, 0, stream>>>(b, k, n, n_main, n_tail, bt, kp);
+  }
   e = cudaGetLastError();
   const int lda = a_ok ? k : kp;
   const int ldb = b_ok ? n : ldb_copy;
