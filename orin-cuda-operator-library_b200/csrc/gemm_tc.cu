@@ -17,7 +17,9 @@
 // tile i overlaps the main loop of tile i+1.  Tiles are walked in groups of
 // 16 M blocks so concurrently running CTAs share A and B panels in L2.
 // B is consumed in its natural row-major (N-major) layout through the
-// descriptor's MN-major mode: no transposed copy.
+// descriptor's MN-major mode: no transposed copy.  When M and N are both at
+// least 256 the CTA-pair version of this kernel (gemm_tc_pair_kernel, 256 x
+// 256 tiles on the two-SM MMA) runs instead.
 //
 // Every mbarrier wait is bounded (tc_common.cuh): a wait that gives up sets
 // the CTA's abort flag and the device watchdog word; the CTA then drains its
@@ -59,10 +61,13 @@ struct Barriers {
 // Work units: tiles [0, tiles_full) whole; each remaining tail tile as two
 // K halves (2 units), so the last wave is two half-length passes instead of
 // one mostly idle full one.  Split units add into C (zeroed beforehand).
-struct TileGrid {
-  int m_blocks, n_blocks, tiles, tiles_full, units, k_blocks;
+// BM: tile height (128, or 256 for a CTA pair); grid_ctas counts CTAs or
+// pairs, whichever runs one tile at a time.
+template <int BM>
+struct TileGridT {
+  int m_blocks, n_blocks, tiles, tiles_full, units, k_blocks, group_m = kGroupM;
   __host__ __device__ void init(int m, int n, int k, int grid_ctas, bool split_tail) {
-    m_blocks = (m + kBM - 1) / kBM;
+    m_blocks = (m + BM - 1) / BM;
     n_blocks = (n + kBN - 1) / kBN;
     tiles = m_blocks * n_blocks;
     k_blocks = (k + kBK - 1) / kBK;
@@ -78,15 +83,16 @@ struct TileGrid {
     kb1 = split && !((u - tiles_full) & 1) ? half : k_blocks;
   }
   __host__ __device__ void coords(int t, int& mb, int& nb) const {
-    const int per_group = kGroupM * n_blocks;
+    const int per_group = group_m * n_blocks;
     const int group = t / per_group;
-    const int first_m = group * kGroupM;
-    const int rows = min(m_blocks - first_m, kGroupM);
+    const int first_m = group * group_m;
+    const int rows = min(m_blocks - first_m, group_m);
     const int local = t - group * per_group;
     mb = first_m + local % rows;
     nb = local / rows;
   }
 };
+using TileGrid = TileGridT<kBM>;
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a,
@@ -273,18 +279,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Zeroes the C tiles [tiles_full, tiles) that the GEMM will build from two
 // K halves added together (0 + a + b is the same in either order, so the
 // result stays deterministic).  One CTA per tile.
+template <int BM>
 __global__ void __launch_bounds__(256)
     zero_tail_tiles_kernel(float* __restrict__ c, int m, int n, int k, int ldc,
-                           int grid_ctas) {
-  // blockIdx.x: tail tile; blockIdx.y: its 8-row slice (16 per tile).
-  TileGrid grid;
+                           int grid_ctas, int group_m) {
+  // blockIdx.x: tail tile; blockIdx.y: its BM/16-row slice (16 per tile).
+  TileGridT<BM> grid;
+  grid.group_m = group_m;
   grid.init(m, n, k, grid_ctas, true);
   int mb, nb;
   grid.coords(grid.tiles_full + blockIdx.x, mb, nb);
   const int col = nb * kBN + threadIdx.x;  // kBN == blockDim.x
   if (col >= n) return;
-  const int row0 = mb * kBM + blockIdx.y * (kBM / 16);
-  const int row_end = min(m, row0 + kBM / 16);
+  const int row0 = mb * BM + blockIdx.y * (BM / 16);
+  const int row_end = min(m, row0 + BM / 16);
 #pragma unroll 8
   for (int row = row0; row < row_end; ++row) c[static_cast<size_t>(row) * ldc + col] = 0.0f;
 }
@@ -364,6 +372,230 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ------------------------------------------------------------------ CTA pairs
+// The same GEMM with the two-SM MMA (tcgen05.mma.cta_group::2, M=256): a
+// cluster of two CTAs computes one 256 x 256 tile, each CTA holding 128 rows
+// of A and 128 columns of B in its shared memory and 128 rows x 256 columns
+// of the accumulator in its TMEM.  Per CTA and K block that is 32 KB of
+// operands instead of 48 KB for the same MMA work, so shared-memory traffic
+// (tensor-core reads plus TMA writes, ~192 B/clk in the one-SM kernel against
+// ~128 B/clk available) no longer caps the tensor pipe.
+//   warp 0 of each CTA  TMA producer for its own halves; completion is
+//            counted on the leader CTA's "full" barrier (pair form of the
+//            load, no multicast), the leader arming it with both CTAs' bytes;
+//   warp 1 of the leader  issues the pair MMAs; its commits arrive on both
+//            CTAs' "empty" / "tmem_full" barriers;
+//   warps 2-5 of each CTA  epilogue of its 128 rows; each warp then arrives
+//            on the leader's "tmem_empty" barrier.
+// A cluster barrier after set-up and before exit keeps each CTA's barriers
+// and TMEM alive while its partner may still use them.
+constexpr int kPairBM = 256;
+constexpr int kPairStages = 6;
+constexpr int kPairABytes = 128 * kBK * 2;   // 16 KB: this CTA's 128 rows of A
+constexpr int kPairBBytes = 2 * kBBoxBytes;  // 16 KB: this CTA's 128 columns of B
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr uint32_t kPairIdesc = tc::idesc_f16_f32(kPairBM, kBN, false, true);
+constexpr size_t kPairSmemBytes =
+    kPairStages * kPairStageBytes + kEpiStageBytes + 1024 + 256;
+constexpr uint16_t kPairMask = 0x3;  // both CTAs of the cluster
+
+struct PairBarriers {
+  uint64_t full[kPairStages];   // leader: both CTAs' loads of a stage
+  uint64_t empty[kPairStages];  // each CTA: the pair MMAs released the stage
+  uint64_t tmem_full[2];        // each CTA: accumulator complete
+  uint64_t tmem_empty[2];       // leader: 8 epilogue warps (both CTAs) done
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_pair_kernel(const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_b, float* __restrict__ c,
+                        int m, int n, int k, int ldc, int split_tail, int group_m,
+                        int* watchdog) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* epi_stage = reinterpret_cast<float*>(smem + kPairStages * kPairStageBytes);
+  PairBarriers* bars =
+      reinterpret_cast<PairBarriers*>(smem + kPairStages * kPairStageBytes + kEpiStageBytes);
+  volatile int* abort = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = tc::cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int pairs = static_cast<int>(gridDim.x >> 1);
+  TileGridT<kPairBM> grid;
+  grid.group_m = group_m;
+  grid.init(m, n, k, pairs, split_tail != 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      tc::mbar_init(&bars->full[s], 1);
+      tc::mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(&bars->tmem_full[b], 1);
+      tc::mbar_init(&bars->tmem_empty[b], 8);
+    }
+    tc::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    tc::fence_barrier_init();
+    tc::prefetch_tmap(&map_a);
+    tc::prefetch_tmap(&map_b);
+  }
+  if (warp == 1) tc::tmem_alloc_pair(&bars->tmem_base, kTmemCols);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // both CTAs' barriers exist before any cross-CTA use
+  tc::tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool issued_any = false;
+    for (int u = pair; u < grid.units && !*abort; u += pairs) {
+      int mb, nb, kb0, kb1;
+      bool split;
+      grid.unit(u, mb, nb, kb0, kb1, split);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!tc::mbar_wait_cluster(&bars->empty[stage], phase ^ 1, abort, watchdog,
+                                   tc::kWatchdogGemm))
+          break;
+        if (leader) tc::mbar_expect_tx(&bars->full[stage], 2 * kPairStageBytes);
+        const uint32_t full_leader = tc::mapa_shared(&bars->full[stage], 0);
+        uint8_t* sa = smem + stage * kPairStageBytes;
+        uint8_t* sb = sa + kPairABytes;
+        tc::tma_load_2d_pair(sa, &map_a, kb * kBK, mb * kPairBM + rank * 128, full_leader);
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          tc::tma_load_2d_pair(sb + j * kBBoxBytes, &map_b, nb * kBN + rank * 128 + j * 64,
+                               kb * kBK, full_leader);
+        issued_any = true;
+        if (++stage == kPairStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+    }
+    if (*abort && issued_any) {
+      // Completions of this CTA's loads are counted on the leader's
+      // barriers; give the copies in flight time to land (bounded).
+      for (int i = 0; i < (1 << 14); ++i) __nanosleep(64);
+    }
+  } else if (warp == 1 && lane == 0 && leader) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    bool issued_any = false;
+    for (int u = pair; u < grid.units && !*abort; u += pairs) {
+      int mb, nb, kb0, kb1;
+      bool split;
+      grid.unit(u, mb, nb, kb0, kb1, split);
+      if (!tc::mbar_wait_cluster(&bars->tmem_empty[acc], acc_phase ^ 1, abort, watchdog,
+                                 tc::kWatchdogGemm))
+        break;
+      tc::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * kBN;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!tc::mbar_wait_cluster(&bars->full[stage], phase, abort, watchdog,
+                                   tc::kWatchdogGemm))
+          break;
+        tc::tc_fence_after();
+        const uint32_t a_addr = tc::smem_u32(smem + stage * kPairStageBytes);
+        const uint32_t b_addr = a_addr + kPairABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          // Same operand layouts as the one-SM kernel, per CTA: A K-major
+          // 128-byte rows (K step 32 B), B N-major 64-column boxes 8 KB
+          // apart (K step two 8-row groups, 2 KB).
+          const uint64_t a_desc = tc::smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+          const uint64_t b_desc = tc::smem_desc_sw128(b_addr + kk * 2048, kBBoxBytes, 1024);
+          tc::umma_f16_pair(d_tmem, a_desc, b_desc, kPairIdesc, (kb != kb0) || (kk != 0));
+        }
+        issued_any = true;
+        tc::umma_commit_pair(&bars->empty[stage], kPairMask);
+        if (++stage == kPairStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (*abort) break;
+      tc::umma_commit_pair(&bars->tmem_full[acc], kPairMask);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    if (*abort && issued_any) {  // wait for issued MMAs before TMEM is freed
+      tc::umma_commit_pair(&bars->drain, 0x1);
+      const uint32_t addr = tc::smem_u32(&bars->drain);
+      for (uint32_t i = 0; i < tc::kMaxPolls; ++i)
+        if (tc::mbar_try_wait(addr, 0)) break;
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    float* stage = epi_stage + (warp - 2) * 32 * kStagePitch;
+    const uint32_t empty_leader0 = tc::mapa_shared(&bars->tmem_empty[0], 0);
+    const uint32_t empty_leader1 = tc::mapa_shared(&bars->tmem_empty[1], 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = pair; u < grid.units; u += pairs) {
+      if (!tc::mbar_wait_cluster_warp(&bars->tmem_full[acc], acc_phase, abort, watchdog,
+                                      tc::kWatchdogGemm))
+        break;
+      tc::tc_fence_after();
+      int mb, nb, kb0, kb1;
+      bool split;
+      grid.unit(u, mb, nb, kb0, kb1, split);
+      const int row0 = mb * kPairBM + static_cast<int>(rank) * 128 + quarter * 32;
+#pragma unroll 1
+      for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+        float v[32];
+        tc::tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN +
+                          chunk * 32,
+                      v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) stage[lane * kStagePitch + i] = v[i];
+        __syncwarp();
+        const int col = nb * kBN + chunk * 32 + lane;
+        if (col < n) {
+          const int rows = min(32, m - row0);
+          if (split) {  // half of a tail tile: add into the zeroed C
+#pragma unroll 4
+            for (int rr = 0; rr < rows; ++rr)
+              atomicAdd(c + static_cast<size_t>(row0 + rr) * ldc + col,
+                        stage[rr * kStagePitch + lane]);
+          } else {
+#pragma unroll 4
+            for (int rr = 0; rr < rows; ++rr)
+              st_stream(c + static_cast<size_t>(row0 + rr) * ldc + col,
+                        stage[rr * kStagePitch + lane]);
+          }
+        }
+        __syncwarp();
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive_cluster(acc == 0 ? empty_leader0 : empty_leader1);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::cluster_sync();  // the partner is done with this CTA's barriers and TMEM
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc_pair(tmem_base, kTmemCols);
+}
+
 cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, int n,
                            int k, int lda, int ldb, int ldc, cudaStream_t stream) {
   CUtensorMap map_a, map_b;
@@ -383,6 +615,41 @@ cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, in
                                 strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (e != cudaSuccess) return e;
   }
+  const int k_blocks = (k + kBK - 1) / kBK;
+  if (m >= kPairBM && n >= kBN && sm_count() >= 2) {
+    // CTA pairs: 256 x 256 tiles, one pair per two SMs.
+    const int group_m = kGroupM;
+    cudaError_t e = cudaFuncSetAttribute(gemm_tc_pair_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kPairSmemBytes));
+    if (e != cudaSuccess) return e;
+    const long long tiles =
+        static_cast<long long>((m + kPairBM - 1) / kPairBM) * ((n + kBN - 1) / kBN);
+    const int max_pairs = sm_count() / 2;
+    const int pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
+    const int tail = static_cast<int>(tiles % pairs);
+    const bool split_tail = tiles > pairs && tail != 0 && 2 * tail <= pairs && k_blocks >= 8;
+    if (split_tail) {
+      zero_tail_tiles_kernel<kPairBM><<<dim3(tail, 16), kBN, 0, stream>>>(c, m, n, k, ldc,
+                                                                          pairs, group_m);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+    }
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    config.blockDim = dim3(kThreads);
+    config.dynamicSmemBytes = kPairSmemBytes;
+    config.stream = stream;
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = 2;
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, gemm_tc_pair_kernel, map_a, map_b, c, m, n, k, ldc,
+                              split_tail ? 1 : 0, group_m, watchdog_word());
+  }
   cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kSmemBytes));
@@ -393,10 +660,10 @@ cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, in
   // Split the tail tiles in K when the last wave would run at most half full
   // (two halves per CTA then still fit in one wave) and K is deep enough.
   const int tail = static_cast<int>(tiles % grid);
-  const bool split_tail = tiles > grid && tail != 0 && 2 * tail <= grid &&
-                          (k + kBK - 1) / kBK >= 8;
+  const bool split_tail = tiles > grid && tail != 0 && 2 * tail <= grid && k_blocks >= 8;
   if (split_tail) {
-    zero_tail_tiles_kernel<<<dim3(tail, 16), kBN, 0, stream>>>(c, m, n, k, ldc, grid);
+    zero_tail_tiles_kernel<kBM><<<dim3(tail, 16), kBN, 0, stream>>>(c, m, n, k, ldc, grid,
+                                                                   kGroupM);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }

@@ -1,7 +1,7 @@
 // sm_100a building blocks for the tensor-core kernels, as inline PTX:
 // mbarriers with bounded waits, TMA tile loads, tcgen05 (TMEM alloc, UMMA,
 // commit, loads) and the shared-memory / instruction descriptors of
-// tcgen05.mma kind::f16.  No cluster multicast anywhere.
+// tcgen05.mma kind::f16.  No TMA load uses cluster multicast.
 #pragma once
 
 #include <cuda.h>
@@ -280,6 +280,120 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 // async proxy (TMA, tensor cores) before it signals an mbarrier.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- CTA pairs
+// Building blocks of the two-SM (cta_group::2) MMA over a cluster of two
+// CTAs.  No cluster multicast of TMA loads: each CTA loads its own operand
+// halves; only tcgen05.commit arrives are multicast to both CTAs.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of all CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+// Shared::cluster address of this CTA's shared variable `p` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// Arrive (release, cluster scope) on an mbarrier given by its cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                   cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_wait with cluster-scope acquire (for barriers that other CTAs of the
+// cluster arrive on); same give-up behaviour.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort, int* watchdog, int code) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t polls = 0; polls < kMaxPolls; ++polls) {
+    if (mbar_try_wait_cluster(addr, parity)) return true;
+    if ((polls & 255u) == 255u && *abort) return false;
+  }
+  *abort = 1;
+  if (watchdog != nullptr) watchdog_trip(watchdog, code);
+  return false;
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster_warp(uint64_t* bar, uint32_t parity,
+                                                       volatile int* abort, int* watchdog,
+                                                       int code) {
+  const bool ok = mbar_wait_cluster(bar, parity, abort, watchdog, code);
+  return __all_sync(kFullMask, ok);
+}
+
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on the mbarrier at cluster address `bar_cluster` (the pair's leader CTA).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+
+// TMEM allocation for both CTAs of the pair: the same warp of each CTA calls
+// it with the same shared-memory slot.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot, uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(slot)),
+               "r"(cols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+               : "memory");
+}
+
+// D (both CTAs' TMEM) (+)= A (each CTA's M/2 rows) * B (each CTA's N/2
+// columns); issued by one thread of the leader CTA.
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier at this CTA-relative offset in every CTA of
+// `cta_mask` when the pair MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 // ---------------------------------------------------------------- descriptors
