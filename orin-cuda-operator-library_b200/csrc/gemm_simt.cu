@@ -9,6 +9,13 @@
 // while the current shared tile is consumed (double-buffered shared memory),
 // one __syncthreads per K step.  Every FMA is a plain FP32 FFMA: no TF32.
 //
+// Work units are tiles in a 1-D grid (row-major over tiles).  When the last
+// wave of resident CTAs (2 per SM) would run at most half full, its tiles
+// are split into two K halves that add into a zeroed C -- 0 + a + b is
+// order-independent, so results stay deterministic -- and the last wave runs
+// two half-length passes instead of one mostly idle full one (4096^3: 1024
+// tiles = 3 x 296 + 136).
+//
 // The same kernel, instantiated for __half inputs (converted to FP32 on the
 // way into shared memory), is the FP16 path for shapes the tensor-core kernel
 // does not take; products of two FP16 values are exact in FP32.
@@ -74,17 +81,37 @@ __device__ __forceinline__ void Quad<__half>::load(const __half* __restrict__ p,
   }
 }
 
+// Zeroes the C tiles [tiles_full, tiles) (row-major over n_tiles columns of
+// tiles); blockIdx.y picks an 8-row slice of the 128-row tile.
+__global__ void __launch_bounds__(kBN)
+    zero_simt_tiles_kernel(float* __restrict__ c, int m, int n, int n_tiles, int tiles_full) {
+  const int t = tiles_full + static_cast<int>(blockIdx.x);
+  const int col = (t % n_tiles) * kBN + static_cast<int>(threadIdx.x);
+  if (col >= n) return;
+  const int row0 = (t / n_tiles) * kBM + static_cast<int>(blockIdx.y) * 8;
+  const int row_end = min(m, row0 + 8);
+  for (int row = row0; row < row_end; ++row) c[static_cast<std::size_t>(row) * n + col] = 0.0f;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 2)
     gemm_simt_kernel(const T* __restrict__ a, const T* __restrict__ b,
                      float* __restrict__ c, int m, int n, int k, bool a_vec,
-                     bool b_vec, bool c_vec) {
+                     bool b_vec, bool c_vec, int n_tiles, int tiles_full) {
   __shared__ __align__(16) float as[2][kBK][kBM];
   __shared__ __align__(16) float bs[2][kBK][kBN];
 
   const int tid = threadIdx.x;
-  const int block_m = blockIdx.y * kBM;
-  const int block_n = blockIdx.x * kBN;
+  const int k_tiles_all = (k + kBK - 1) / kBK;
+  // Unit -> tile and K-tile range (a split unit covers one K half).
+  const int u = static_cast<int>(blockIdx.x);
+  const bool split = u >= tiles_full;
+  const int tile = split ? tiles_full + ((u - tiles_full) >> 1) : u;
+  const int k_half = k_tiles_all / 2;
+  const int kt_begin = split && ((u - tiles_full) & 1) ? k_half : 0;
+  const int kt_end = split && !((u - tiles_full) & 1) ? k_half : k_tiles_all;
+  const int block_m = (tile / n_tiles) * kBM;
+  const int block_n = (tile % n_tiles) * kBN;
 
   // Global-load assignment: A quad = row tid/2, k offset 4*(tid%2);
   // B quad = k row tid/32, n offset 4*(tid%32).
@@ -123,13 +150,12 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
     for (int p = 0; p < 4; ++p) acc2[i][p] = 0;  // (+0.0f, +0.0f)
 
-  const int k_tiles = (k + kBK - 1) / kBK;
-  fetch(0);
+  fetch(kt_begin * kBK);
   stash(0);
   __syncthreads();
-  for (int t = 0; t < k_tiles; ++t) {
-    const int buf = t & 1;
-    if (t + 1 < k_tiles) fetch((t + 1) * kBK);
+  for (int t = kt_begin; t < kt_end; ++t) {
+    const int buf = (t - kt_begin) & 1;
+    if (t + 1 < kt_end) fetch((t + 1) * kBK);
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
       float af[8];
@@ -147,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int p = 0; p < 4; ++p) fma2(acc2[i][p], a2, bp[p]);
       }
     }
-    if (t + 1 < k_tiles) stash(buf ^ 1);
+    if (t + 1 < kt_end) stash(buf ^ 1);
     __syncthreads();
   }
 
@@ -165,7 +191,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int half = 0; half < 2; ++half) {
       const int col = block_n + half * 64 + tx * 4;
       const float* v = &acc[i][half * 4];
-      if (c_vec && col + 3 < n) {
+      if (split) {  // half of a tail tile: add into the zeroed C
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (col + j < n) atomicAdd(crow + col + j, v[j]);
+      } else if (c_vec && col + 3 < n) {
         *reinterpret_cast<float4*>(crow + col) = make_float4(v[0], v[1], v[2], v[3]);
       } else {
 #pragma unroll
@@ -185,10 +215,23 @@ cudaError_t gemm_simt(const T* a, const T* b, float* c, int m, int n, int k,
   const bool a_vec = (k % 4 == 0) && ((reinterpret_cast<std::uintptr_t>(a) % (4 * elem)) == 0);
   const bool b_vec = (n % 4 == 0) && ((reinterpret_cast<std::uintptr_t>(b) % (4 * elem)) == 0);
   const bool c_vec = (n % 4 == 0) && aligned16(c);
-  const dim3 grid((n + kBN - 1) / kBN, (m + kBM - 1) / kBM);
-  if (grid.y > 65535) return cudaErrorInvalidValue;
-  gemm_simt_kernel<T><<<grid, kThreads, 0, stream>>>(a, b, c, m, n, k, a_vec,
-                                                     b_vec, c_vec);
+  const long long n_tiles = (n + kBN - 1) / kBN;
+  const long long tiles = n_tiles * ((m + kBM - 1) / kBM);
+  const long long slots = 2LL * sm_count();  // resident CTAs (launch bounds: 2 per SM)
+  const long long tail = tiles % slots;
+  const bool split = tiles > slots && tail != 0 && 2 * tail <= slots && k >= 16 * kBK;
+  const long long tiles_full = split ? tiles - tail : tiles;
+  const long long units = tiles_full + (split ? 2 * tail : 0);
+  if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (split) {
+    zero_simt_tiles_kernel<<<dim3(static_cast<unsigned>(tail), kBM / 8), kBN, 0, stream>>>(
+        c, m, n, static_cast<int>(n_tiles), static_cast<int>(tiles_full));
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  gemm_simt_kernel<T><<<static_cast<unsigned>(units), kThreads, 0, stream>>>(
+      a, b, c, m, n, k, a_vec, b_vec, c_vec, static_cast<int>(n_tiles),
+      static_cast<int>(tiles_full));
   return cudaGetLastError();
 }
 

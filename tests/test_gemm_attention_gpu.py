@@ -68,7 +68,30 @@ def test_gemm_f16(cuda, stream, m, n, k):
 
 GEMM_F32 = [(1, 256, 64), (16, 128, 64), (128, 64, 32), (37, 65, 71),  # ref tests
             (7, 37, 23), (128, 128, 8), (1, 1, 1), (513, 257, 129),
-            (1024, 1024, 1024), (4095, 4097, 4093)]
+            (1024, 1024, 1024), (4095, 4097, 4093),
+            # > 2 tiles per SM with a small last wave: K-split tail tiles
+            (2048, 2560, 256), (2048, 2600, 200)]
+
+
+def test_gemm_f32_split_tail_deterministic(cuda, stream):
+    """Tail tiles computed as two K halves added into a zeroed C: repeat
+    runs are bit-identical."""
+    import torch
+
+    rng = np.random.default_rng(5)
+    m, n, k = 2048, 2560, 512
+    a = torch.from_numpy((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32)).to(cuda)
+    b = torch.from_numpy((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)).to(cuda)
+    outs = []
+    for _ in range(3):
+        c = torch.full((m, n), float("nan"), device=cuda)
+        operatorlib.gemm_into(a, b, c)
+        outs.append(c)
+    stream.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+    idx = np.unique(np.linspace(0, m - 1, 64).astype(int))
+    want = a.cpu().numpy()[idx].astype(np.float64) @ b.cpu().numpy().astype(np.float64)
+    np.testing.assert_allclose(outs[0].cpu().numpy()[idx], want, rtol=1e-3, atol=1e-3)
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_F32)
