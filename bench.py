@@ -776,6 +776,37 @@ def cpu_baseline_record() -> dict:
                       f"median step {sec * 1e3:.1f} ms, rows split over {cpu.threads} threads"}
 
 
+def cpu_torch_record(budget_s: float = 5.0, max_steps: int = 100) -> dict:
+    """The torch CPU equivalents of the headline step (the reference's
+    python/test_extension.py:17-27 references: torch.softmax, the RMSNorm
+    formula, t().contiguous()), at torch's own host thread count -- reported
+    beside the reference's C loops, not used as the baseline."""
+    import torch
+
+    rng = np.random.default_rng(4242)
+    sm, rx, rw, tx = (torch.from_numpy(a) for a in gen_rowops(rng))
+
+    def step():
+        torch.softmax(sm, dim=-1)
+        rx * torch.rsqrt(rx.pow(2).mean(dim=-1, keepdim=True) + RMS_EPS) * rw
+        tx.t().contiguous()
+
+    step()
+    times = []
+    t_start = time.perf_counter()
+    while len(times) < max_steps:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    sec = statistics.median(times)
+    return {"value": round(STEP_BYTES / sec / 1e9, 3), "unit": "GB/s",
+            "cores": torch.get_num_threads(), "kind": "torch-cpu",
+            "sample": f"{len(times)} full headline steps through torch CPU ops, "
+                      f"median step {sec * 1e3:.1f} ms"}
+
+
 # ------------------------------------------------------------ main
 
 def committed_traffic(kernel: str):
@@ -841,6 +872,8 @@ def run_ours(args, dist) -> int:
     watchdog = ctypes_int.value if code == 0 else f"read failed ({code})"
     cpu = (cpu_baseline_record() if (dist.rank == 0 and dist.world == 1 and not args.no_cpu)
            else None)
+    cpu_torch = (cpu_torch_record()
+                 if (dist.rank == 0 and dist.world == 1 and not args.no_cpu) else None)
     if dist.rank == 0:
         value = STEP_BYTES * dist.world / (head["ms"] * 1e-3) / 1e9
         e2e = STEP_BYTES * dist.world / (head["e2e_ms"] * 1e-3) / 1e9
@@ -878,6 +911,8 @@ def run_ours(args, dist) -> int:
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if cpu_torch is not None:
+            line["cpu_torch"] = cpu_torch
         if ops:
             line["ops"] = ops
         if ref is not None:
