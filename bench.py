@@ -776,6 +776,118 @@ def cpu_baseline_record() -> dict:
                       f"median step {sec * 1e3:.1f} ms, rows split over {cpu.threads} threads"}
 
 
+def cpu_ops_records(budget_s: float = 1.5) -> dict:
+    """CPU figures beside the per-config GPU numbers: the reference's C loops
+    (oracle/_ref, kind "reference") for reduce, the ragged row ops and
+    attention, torch CPU matmul (the reference's own GEMM check) for GEMMs.
+    Work too large for a short budget runs on a slice (rows of A, heads of
+    attention) and is scaled linearly; such records say "extrapolated"."""
+    import torch
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle import oracle as orc
+
+    ref = orc.ref_cpu()
+    kind = "reference" if ref is not None else "port"
+    L = ref if ref is not None else orc.lib()
+    F = orc._fp
+    threads = orc.cpu_threads()
+    pool = ThreadPoolExecutor(threads)
+    rng = np.random.default_rng(77)
+    out = {}
+
+    def timed(fn):
+        fn()
+        times, t_start = [], time.perf_counter()
+        while True:
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+            if time.perf_counter() - t_start > budget_s or len(times) >= 50:
+                return statistics.median(times), len(times)
+
+    def rec(name, value, unit, cores, knd, sample, extrapolated=False):
+        r = {"value": round(value, 4), "unit": unit, "cores": cores, "kind": knd,
+             "sample": sample}
+        if extrapolated:
+            r["extrapolated"] = True
+        out[name] = r
+
+    def split_rows(rows, fn):
+        jobs = [pool.submit(fn, r0, r1) for r0, r1 in
+                (shard_range(rows, threads, i) for i in range(threads)) if r1 > r0]
+        for j in jobs:
+            j.result()
+
+    # reduce 16M
+    n = 16_777_216
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    red = L.ref_cpu_reduce_sum if ref is not None else L.oracle_reduce_sum
+    sec, k = timed(lambda: split_rows(n, lambda a, b: red(F(x[a:]), b - a)))
+    rec("reduce_16M", n * 4 / sec / 1e9, "GB/s", threads, kind, f"{k} full runs, chunks per thread")
+
+    # ragged row ops 4097 x 1023
+    r, c = 4097, 1023
+    xr = rng.normal(0, 2, (r, c)).astype(np.float32)
+    w = rng.normal(1, 0.1, c).astype(np.float32)
+    y = np.empty_like(xr)
+    soft = L.ref_cpu_softmax if ref is not None else L.oracle_softmax
+    rms = L.ref_cpu_rmsnorm if ref is not None else L.oracle_rmsnorm
+    tra = L.ref_cpu_transpose if ref is not None else L.oracle_transpose
+    sec, k = timed(lambda: split_rows(r, lambda a, b: soft(F(xr[a:]), F(y[a:]), b - a, c)))
+    rec("softmax_4097x1023", 2 * r * c * 4 / sec / 1e9, "GB/s", threads, kind, f"{k} full runs")
+    sec, k = timed(lambda: split_rows(
+        r, lambda a, b: rms(F(xr[a:]), F(w), F(y[a:]), b - a, c, RMS_EPS)))
+    rec("rmsnorm_4097x1023", (2 * r * c + c) * 4 / sec / 1e9, "GB/s", threads, kind,
+        f"{k} full runs")
+
+    def tpart(a, b):
+        tmp = np.empty((c, b - a), dtype=np.float32)
+        tra(F(xr[a:]), F(tmp), b - a, c)
+    sec, k = timed(lambda: split_rows(r, tpart))
+    rec("transpose_4097x1023", 2 * r * c * 4 / sec / 1e9, "GB/s", threads, kind, f"{k} full runs")
+
+    # attention B1 H12 S1024 D128: one head per thread, heads sliced
+    s_, d_ = 1024, 128
+    heads = min(threads, 12)
+    q, kk, v = (rng.normal(0, 1, (heads, s_, d_)).astype(np.float32) for _ in range(3))
+    o = np.empty_like(q)
+    if ref is not None:
+        for causal in (0, 1):
+            def att():
+                jobs = [pool.submit(ref.ref_cpu_attention, F(q[h]), F(kk[h]), F(v[h]), F(o[h]),
+                                    1, 1, s_, d_, causal) for h in range(heads)]
+                for j in jobs:
+                    j.result()
+            sec, k = timed(att)
+            flops = (2.0 * heads * d_ * s_ * (s_ + 1)) if causal else 4.0 * heads * s_ * s_ * d_
+            for tag in ("f16", "f32"):
+                rec(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}",
+                    flops / sec / 1e12, "TFLOP/s", heads, kind,
+                    f"{heads} of 12 heads (one per thread), {k} runs; rate scales with "
+                    f"heads up to the core count", extrapolated=heads < 12)
+
+    # GEMMs through torch CPU matmul (FP32 math), a row slice of A
+    tt = torch.get_num_threads()
+    for name, (m, nn, kd), rows in (("gemm_f16_4096", (4096, 4096, 4096), 64),
+                                    ("gemm_f32_4096", (4096, 4096, 4096), 64),
+                                    ("gemm_f16_4095x4097x4093", (4095, 4097, 4093), 64),
+                                    ("gemm_f16_m1_4096x4096", (1, 4096, 4096), 1),
+                                    ("gemm_f16_m16_4096x4096", (16, 4096, 4096), 16)):
+        a_ = torch.from_numpy(rng.uniform(-1, 1, (rows, kd)).astype(np.float32))
+        b_ = torch.from_numpy(rng.uniform(-1, 1, (kd, nn)).astype(np.float32))
+        sec, k = timed(lambda: torch.matmul(a_, b_))
+        if "_m" in name:
+            rec(name, (2 * (rows * kd + kd * nn) + 4 * rows * nn) / sec / 1e9, "GB/s", tt,
+                "torch-cpu", f"torch.matmul FP32, {k} runs")
+        else:
+            rec(name, 2.0 * rows * nn * kd / sec / 1e12, "TFLOP/s", tt, "torch-cpu",
+                f"torch.matmul FP32 on {rows} of {m} rows, {k} runs, scaled",
+                extrapolated=True)
+    pool.shutdown()
+    return out
+
+
 def cpu_torch_record(budget_s: float = 5.0, max_steps: int = 100) -> dict:
     """The torch CPU equivalents of the headline step (the reference's
     python/test_extension.py:17-27 references: torch.softmax, the RMSNorm
@@ -913,6 +1025,10 @@ def run_ours(args, dist) -> int:
             line["cpu_baseline"] = cpu
         if cpu_torch is not None:
             line["cpu_torch"] = cpu_torch
+        if ops and dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+            for name, r in cpu_ops_records().items():
+                if name in ops:
+                    ops[name]["cpu"] = r
         if ops:
             line["ops"] = ops
         if ref is not None:
