@@ -156,7 +156,7 @@ class ClockSampler:
     """Samples the SM clock and throttle reasons of this rank's GPU through
     NVML every `period` seconds on a background thread (reading only)."""
 
-    def __init__(self, torch_device: int, period: float = 0.01):
+    def __init__(self, torch_device: int, period: float = 0.002):
         self.period = period
         self.samples: list[tuple[float, int, int]] = []
         self.max_mhz = None
@@ -207,8 +207,10 @@ class ClockSampler:
                     "note": getattr(self, "error", "nvml unavailable")}
         window = [s for s in self.samples
                   if (t0 is None or s[0] >= t0) and (t1 is None or s[0] <= t1)]
-        if not window:
+        where = "timed region"
+        if len(window) < 5:  # timed region shorter than a few sampling periods
             window = self.samples
+            where = "whole benchmark run (timed region shorter than 5 sampling periods)"
         busy = [s for s in window if not (s[2] & REASON_BITS["gpu_idle"])] or window
         mask = 0
         for s in busy:
@@ -216,7 +218,7 @@ class ClockSampler:
         reasons = [k for k, bit in REASON_BITS.items() if mask & bit and k != "gpu_idle"]
         return {"sm_mhz": statistics.median(s[1] for s in busy) if busy else None,
                 "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(busy)}
+                "samples": len(busy), "window": where}
 
 
 # ------------------------------------------------------------ timing helpers
