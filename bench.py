@@ -869,8 +869,20 @@ def cpu_ops_records(budget_s: float = 1.5) -> dict:
                     f"{heads} of 12 heads (one per thread), {k} runs; rate scales with "
                     f"heads up to the core count", extrapolated=heads < 12)
 
-    # GEMMs through torch CPU matmul (FP32 math), a row slice of A
+    # BF16 row ops through torch CPU (the reference has no 16-bit row ops)
     tt = torch.get_num_threads()
+    xb = torch.from_numpy(rng.normal(0, 1, (4096, 1024)).astype(np.float32)).to(torch.bfloat16)
+    sec, k = timed(lambda: torch.softmax(xb, dim=-1))
+    rec("softmax_bf16_4096x1024", 2 * xb.numel() * 2 / sec / 1e9, "GB/s", tt, "torch-cpu",
+        f"torch.softmax BF16, {k} runs")
+    xr16 = torch.from_numpy(rng.normal(0, 1, (2048, 4096)).astype(np.float32)).to(torch.bfloat16)
+    wr16 = torch.ones(4096, dtype=torch.bfloat16)
+    sec, k = timed(lambda: xr16 * torch.rsqrt(xr16.float().pow(2).mean(-1, keepdim=True)
+                                              + RMS_EPS).to(torch.bfloat16) * wr16)
+    rec("rmsnorm_bf16_2048x4096", (2 * xr16.numel() + 4096) * 2 / sec / 1e9, "GB/s", tt,
+        "torch-cpu", f"RMSNorm formula in torch BF16 (FP32 sum of squares), {k} runs")
+
+    # GEMMs through torch CPU matmul (FP32 math), a row slice of A
     for name, (m, nn, kd), rows in (("gemm_f16_4096", (4096, 4096, 4096), 64),
                                     ("gemm_f32_4096", (4096, 4096, 4096), 64),
                                     ("gemm_f16_4095x4097x4093", (4095, 4097, 4093), 64),
