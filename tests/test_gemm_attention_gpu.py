@@ -125,7 +125,7 @@ ATT_CASES = [  # (B, H, S, D, causal, qk range)
     (1, 2, 200, 128, True, 1.0), (1, 4, 256, 64, True, 1.0), (2, 2, 513, 96, False, 1.0),
     (1, 12, 1024, 128, False, None), (1, 12, 1024, 128, True, None),  # BASELINE
     (1, 1, 2048, 128, True, None), (1, 2, 1536, 64, False, None),   # many KV splits
-    (1, 1, 1000, 128, True, None),
+    (1, 1, 1000, 128, True, None), (1, 3, 640, 64, True, None),  # causal key-range parts
 ]
 
 
