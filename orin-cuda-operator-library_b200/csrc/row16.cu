@@ -204,12 +204,17 @@ struct Shape16 {
 // Smallest register-cached shape holding `count` slots (uint4 of 8 elements
 // when vec, single elements otherwise); false when the row is too long.
 bool pick16(int count, bool vec, Shape16* s) {
-  static const Shape16 kVec[] = {{32, 128, 1}, {32, 128, 2}, {32, 128, 4},
+  // {128, 128, 4}: one 4096-wide row per 128-thread CTA, 32 floats per
+  // thread -- small enough for 16 CTAs per SM, so a 2048-row call is in
+  // flight in one wave.
+  static const Shape16 kVec[] = {{32, 128, 1},  {32, 128, 2},   {32, 128, 4},    {128, 128, 4},
                                  {256, 256, 4}, {256, 256, 8}, {1024, 1024, 4}};
   static const Shape16 kScalar[] = {{32, 128, 1}, {32, 128, 4}, {32, 128, 16}, {32, 128, 32},
                                     {256, 256, 32}, {1024, 1024, 32}};
   const Shape16* table = vec ? kVec : kScalar;
-  for (int i = 0; i < 6; ++i)
+  const int entries = vec ? static_cast<int>(sizeof(kVec) / sizeof(kVec[0]))
+                          : static_cast<int>(sizeof(kScalar) / sizeof(kScalar[0]));
+  for (int i = 0; i < entries; ++i)
     if (static_cast<long long>(table[i].group) * table[i].items >= count) {
       *s = table[i];
       return true;
@@ -223,6 +228,7 @@ bool pick16(int count, bool vec, Shape16* s) {
       if (s.group == 32 && s.items == 1) BODY(32, 128, 1, true)                  \
       else if (s.group == 32 && s.items == 2) BODY(32, 128, 2, true)             \
       else if (s.group == 32) BODY(32, 128, 4, true)                             \
+      else if (s.group == 128) BODY(128, 128, 4, true)                           \
       else if (s.group == 256 && s.items == 4) BODY(256, 256, 4, true)           \
       else if (s.group == 256) BODY(256, 256, 8, true)                           \
       else BODY(1024, 1024, 4, true)                                             \
