@@ -119,6 +119,7 @@ SOFTMAX_CASES = [
     (1, 1, 1.0), (3, 7, 1.0), (33, 33, 3.0), (8, 2048, 2.0), (5, 4100, 2.0),
     (3, 8192, 2.0), (2, 16383, 2.0), (2, 32768, 2.0), (2, 40000, 2.0),
     (1, 100_003, 2.0),
+    (5, 5, 2.0), (11, 130, 2.0), (6, 2047, 2.0), (9, 2163, 2.0),  # ragged float4 windows
 ]
 
 
@@ -163,7 +164,8 @@ RMS_CASES = [(32, 4096), (17, 1003), (3 * 7, 1024), (5, 1003),  # reference test
              (2048, 4096),                                       # BASELINE
              (4097, 1023),                                       # ragged
              (1, 1), (9, 3), (4, 64), (7, 8192), (3, 16384), (2, 30001),
-             (2, 32768), (2, 40000), (1, 131_072)]
+             (2, 32768), (2, 40000), (1, 131_072),
+             (4, 5), (13, 513), (6, 2047), (9, 2163)]  # ragged float4 windows
 
 
 @pytest.mark.parametrize("tokens,hidden", RMS_CASES)
