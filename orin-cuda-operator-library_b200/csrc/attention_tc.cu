@@ -98,6 +98,25 @@ __device__ __forceinline__ void bar_sync_named(int count) {
   asm volatile("bar.sync 1, %0;" ::"r"(count) : "memory");
 }
 
+__device__ __forceinline__ uint64_t f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void split_f32x2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 __device__ __forceinline__ float pack_half2_bits(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return __uint_as_float(*reinterpret_cast<const uint32_t*>(&h));
@@ -377,12 +396,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       // independent partial sums.  Measured on B200, MUFU throughput is the
       // softmax's limit; an FMA-pipe polynomial for part of the keys cost
       // more issue slots than it saved.
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // Scale-and-shift and the row sum on packed FP32 pairs (fma.rn.f32x2 /
+      // add.rn.f32x2: two IEEE FP32 operations per instruction), halving
+      // their issue slots next to the MUFU exponentials.
+      uint64_t ps2[4] = {0, 0, 0, 0};
+      const uint64_t scale2 = f32x2(scale_log2, scale_log2);
+      const uint64_t shift2 = f32x2(-m_used, -m_used);
 #pragma unroll
-      for (int i = 0; i < kKeys; ++i) {
-        s[i] = fast_exp2(fmaf(s[i], scale_log2, -m_used));  // -inf -> 0
-        ps[i & 7] += s[i];
+      for (int i = 0; i < kKeys / 2; ++i) {
+        float x0, x1;
+        split_f32x2(fma_f32x2(f32x2(s[2 * i], s[2 * i + 1]), scale2, shift2), x0, x1);
+        s[2 * i] = fast_exp2(x0);  // -inf -> 0
+        s[2 * i + 1] = fast_exp2(x1);
+        ps2[i & 3] = add_f32x2(ps2[i & 3], f32x2(s[2 * i], s[2 * i + 1]));
       }
+      float ps[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split_f32x2(ps2[k], ps[2 * k], ps[2 * k + 1]);
       l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       // P as packed FP16 pairs (packed in place, front to back) into the
       // first 64 columns of S_x.
