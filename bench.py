@@ -278,6 +278,10 @@ def graph_ms_per_launch(fn, launches: int, reps: int, dist, stream) -> float:
 
 # ------------------------------------------------------------ headline: row ops
 
+WORKLOAD = ("rowops_f32: softmax 4096x1024 x~N(0,2^2) + rmsnorm 2048x4096 x~N(0,1), "
+            "w~N(1,0.1), eps 1e-6 + transpose 4096x4096 U[-1,1)")
+
+
 def gen_rowops(rng, rows_scale: int = 1):
     """BASELINE configs[1] inputs (host, float32)."""
     sm = rng.normal(0, 2, SOFTMAX_SHAPE).astype(np.float32)
@@ -962,8 +966,7 @@ def run_reference(args, dist) -> int:
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "rowops_f32: softmax 4096x1024 + rmsnorm 2048x4096 "
-                               "+ transpose 4096x4096", "device": "host CPU"},
+        "config": {"workload": WORKLOAD, "device": "host CPU"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cpu.threads,
                          "kind": cpu.kind,
                          "sample": f"{args.steps} full workload steps after {args.warmup} warm-up"},
@@ -1011,8 +1014,7 @@ def run_ours(args, dist) -> int:
             "ms_per_step": round(head["ms"], 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {
-                "workload": "rowops_f32: softmax 4096x1024 N(0,4) + rmsnorm 2048x4096 "
-                            "N(0,1), w N(1,0.01), eps 1e-6 + transpose 4096x4096 U[-1,1)",
+                "workload": WORKLOAD,
                 "per_rank": "each rank owns its own full row set (row-sharded, no collective)",
                 "l2": f"inputs rotate over {head['n_sets']} buffer sets "
                       f"({head['n_sets'] * STEP_BYTES / 2**20:.0f} MiB > 2x L2)",
