@@ -537,7 +537,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         ms = _measure(lambda i, h: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
         record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
 
-    # 16-bit I/O row ops (SURVEY row F3): BF16 softmax 4096x1024, RMSNorm 2048x4096
+    # 16-bit I/O row ops: BF16 softmax 4096x1024, RMSNorm 2048x4096
     if want("row16"):
         for tag, fn, (r, c) in [("softmax_bf16_4096x1024", lib.opl_softmax_bf16, SOFTMAX_SHAPE),
                                 ("rmsnorm_bf16_2048x4096", lib.opl_rmsnorm_bf16, RMS_SHAPE)]:
@@ -572,7 +572,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         record(name, ms, 2.0 * m * n * k, "tensor" if dtype == np.float16 else "ffma",
                peak, "TFLOP/s", world_units=dist.world)
 
-    # skinny FP16 GEMM (decode shapes, BASELINE-adjacent SURVEY row F1):
+    # skinny FP16 GEMM (decode shapes):
     # bound by streaming B, reported as GB/s of A + B + C
     if want("gemv"):
         for m in (1, 16):
