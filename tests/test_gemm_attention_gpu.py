@@ -140,6 +140,19 @@ def att_inputs(shape, qk, seed, dtype):
     return [x.astype(dtype) for x in (q, k, v)]
 
 
+@pytest.mark.parametrize("h,s,d", [(100, 520, 64), (80, 1000, 128)])
+def test_attention_f16_pairs_causal(cuda, stream, h, s, d):
+    """Grids with B*H*(query tiles / 2) >= 2 x SMs run two query tiles per
+    CTA (the sharded-config path); causal with a ragged last tile.  A few
+    heads spread over the batch are checked against the oracle."""
+    q, k, v = att_inputs((1, h, s, d), None, h + s + d, np.float16)
+    got = run_attention(cuda, stream, q, k, v, True)
+    heads = [0, h // 3, h // 2 + 1, h - 1]
+    want = orc.attention(q[:, heads].astype(np.float32), k[:, heads].astype(np.float32),
+                         v[:, heads].astype(np.float32), True)
+    check_f16(got[:, heads], want)
+
+
 @pytest.mark.parametrize("b,h,s,d,causal,qk", ATT_CASES)
 def test_attention_f16(cuda, stream, b, h, s, d, causal, qk):
     q, k, v = att_inputs((b, h, s, d), qk, s * 3 + d, np.float16)
