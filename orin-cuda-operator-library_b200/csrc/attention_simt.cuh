@@ -12,8 +12,9 @@ cudaError_t attention_simt(const T* q, const T* k, const T* v, float* out,
                            int batch, int heads, int seq, int d, bool causal,
                            cudaStream_t stream);
 
-// tcgen05 FP16 attention (FP32 state and output) for head_dim 64 or 128 with
-// 16-byte aligned tensors; attention_tc_supported says whether it applies.
+// tcgen05 FP16 attention (FP32 state and output) for head_dim <= 128 with
+// head_dim % 8 == 0 (computed as 64 or 128 with zero padding) and 16-byte
+// aligned tensors; attention_tc_supported says whether it applies.
 bool attention_tc_supported(int head_dim, const void* q, const void* k, const void* v,
                             const void* out);
 cudaError_t attention_f16_tc(const __half* q, const __half* k, const __half* v, float* out,

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         const __grid_constant__ CUtensorMap map_k,
                         const __grid_constant__ CUtensorMap map_v,
                         const __grid_constant__ CUtensorMap map_o,
-                        int heads_total, int seq, int causal, float scale_log2,
+                        int heads_total, int seq, int head_dim, int causal, float scale_log2,
                         int tiles_per_cta, int* watchdog) {
   using Cfg = AttnCfg<D>;
   extern __shared__ uint8_t smem_raw[];
@@ -482,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
           tc::fence_proxy_async_smem();
           __syncwarp();
-          if (lane == 0 && y0 < seq) {
+          if (lane == 0 && y0 < seq && col < head_dim) {  // columns >= head_dim: padding
             tc::tma_store_3d(&map_o, buf, col, y0, bh);
             tc::bulk_commit();
           }
@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           o[4 * k + 3] * inv);
         tc::fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0 && y0 < seq) {
+        if (lane == 0 && y0 < seq && c * 32 < head_dim) {  // columns >= head_dim: padding
           tc::tma_store_3d(&map_o, buf, c * 32, y0, bh);
           tc::bulk_commit();
         }
@@ -530,17 +530,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
 }
 
+// D is the padded head dimension the kernel computes with (64 or 128);
+// head_dim <= D (a multiple of 8) is the caller's: the tensor maps have
+// head_dim columns, so TMA fills columns head_dim .. D-1 of Q, K and V with
+// zeros (they add nothing to Q K^T, and give O columns that are not stored).
 template <int D>
 cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* v,
-                                float* out, int heads_total, int seq, bool causal,
+                                float* out, int heads_total, int seq, int head_dim, bool causal,
                                 cudaStream_t stream) {
   using Cfg = AttnCfg<D>;
   CUtensorMap maps[4];
   const __half* ptrs[3] = {q, k, v};
-  const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(seq),
+  const uint64_t dims[3] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(seq),
                             static_cast<uint64_t>(heads_total)};
-  const uint64_t strides[2] = {static_cast<uint64_t>(D) * 2,
-                               static_cast<uint64_t>(D) * 2 * seq};
+  const uint64_t strides[2] = {static_cast<uint64_t>(head_dim) * 2,
+                               static_cast<uint64_t>(head_dim) * 2 * seq};
   const uint32_t box[3] = {64, 128, 1};
   for (int i = 0; i < 3; ++i) {
     const cudaError_t e = encode_tmap(&maps[i], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, ptrs[i],
@@ -548,8 +552,8 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
     if (e != cudaSuccess) return e;
   }
   {  // O: FP32 [B*H, S, D], 32 x 32 store boxes
-    const uint64_t o_strides[2] = {static_cast<uint64_t>(D) * 4,
-                                   static_cast<uint64_t>(D) * 4 * seq};
+    const uint64_t o_strides[2] = {static_cast<uint64_t>(head_dim) * 4,
+                                   static_cast<uint64_t>(head_dim) * 4 * seq};
     const uint32_t o_box[3] = {32, 32, 1};
     const cudaError_t e = encode_tmap(&maps[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, dims,
                                       o_strides, o_box, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -567,7 +571,7 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
   const long long ctas =
       static_cast<long long>(heads_total) * ((q_tiles + tiles_per_cta - 1) / tiles_per_cta);
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(D));
+  const float scale_log2 = 1.4426950408889634f / sqrtf(static_cast<float>(head_dim));
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(static_cast<unsigned>(ctas));
   config.blockDim = dim3(kThreads);
@@ -579,7 +583,7 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
   config.attrs = attribute;
   config.numAttrs = 1;
   return cudaLaunchKernelEx(&config, attention_tc_kernel<D>, maps[0], maps[1], maps[2], maps[3],
-                            heads_total, seq, causal ? 1 : 0, scale_log2, tiles_per_cta,
+                            heads_total, seq, head_dim, causal ? 1 : 0, scale_log2, tiles_per_cta,
                             watchdog_word());
 }
 
@@ -587,8 +591,9 @@ cudaError_t launch_attention_tc(const __half* q, const __half* k, const __half* 
 
 bool attention_tc_supported(int head_dim, const void* q, const void* k, const void* v,
                             const void* out) {
-  return (head_dim == 64 || head_dim == 128) && aligned16(q) && aligned16(k) &&
-         aligned16(v) && aligned16(out);
+  // Any head_dim <= 128 with 16-byte rows: computed as 64 or 128 (zero padding).
+  return head_dim >= 8 && head_dim <= 128 && head_dim % 8 == 0 && aligned16(q) &&
+         aligned16(k) && aligned16(v) && aligned16(out);
 }
 
 cudaError_t attention_f16_tc(const __half* q, const __half* k, const __half* v, float* out,
@@ -596,9 +601,11 @@ cudaError_t attention_f16_tc(const __half* q, const __half* k, const __half* v, 
                              cudaStream_t stream) {
   const long long total = static_cast<long long>(batch) * heads;
   if (total > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (head_dim == 128)
-    return launch_attention_tc<128>(q, k, v, out, static_cast<int>(total), seq, causal, stream);
-  return launch_attention_tc<64>(q, k, v, out, static_cast<int>(total), seq, causal, stream);
+  if (head_dim > 64)
+    return launch_attention_tc<128>(q, k, v, out, static_cast<int>(total), seq, head_dim, causal,
+                                    stream);
+  return launch_attention_tc<64>(q, k, v, out, static_cast<int>(total), seq, head_dim, causal,
+                                 stream);
 }
 
 }  // namespace opl
