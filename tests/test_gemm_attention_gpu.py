@@ -126,6 +126,8 @@ ATT_CASES = [  # (B, H, S, D, causal, qk range)
     (1, 12, 1024, 128, False, None), (1, 12, 1024, 128, True, None),  # BASELINE
     (1, 1, 2048, 128, True, None), (1, 2, 1536, 64, False, None),   # many KV splits
     (1, 1, 1000, 128, True, None), (1, 3, 640, 64, True, None),  # causal key-range parts
+    (1, 4, 300, 32, True, None), (1, 2, 700, 80, False, None),     # head_dim padded to
+    (2, 2, 129, 120, True, None),                                  # 64 / 128 by TMA
 ]
 
 
