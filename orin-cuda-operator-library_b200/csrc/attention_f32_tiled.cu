@@ -61,7 +61,7 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_f32_tiled_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                const float* __restrict__ v, float* __restrict__ out,
-                               int heads_total, int seq, int causal, float scale,
+                               int heads_total, int seq, int hd, int causal, float scale,
                                int splits, float* __restrict__ part_o,
                                float2* __restrict__ part_ml) {
   using Cfg = F32Cfg<D>;
@@ -77,7 +77,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = rest % heads_total;
   const int qb = q_blocks - 1 - rest / heads_total;
   const int q0 = qb * kBM;
-  const size_t base = static_cast<size_t>(bh) * seq * D;
+  // hd <= D: the caller's head_dim; columns hd .. D-1 are zero padding.
+  const size_t base = static_cast<size_t>(bh) * seq * hd;
   const int tid = threadIdx.x;
   const int tr = tid >> 4;
   const int tc = tid & 15;
@@ -87,8 +88,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = idx % kBM;
     const int c4 = idx / kBM;
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + row < seq)
-      x = __ldg(reinterpret_cast<const float4*>(q + base + static_cast<size_t>(q0 + row) * D) + c4);
+    if (q0 + row < seq && 4 * c4 < hd)
+      x = __ldg(reinterpret_cast<const float4*>(q + base + static_cast<size_t>(q0 + row) * hd) + c4);
     qt[(4 * c4 + 0) * Cfg::kQPitch + row] = x.x;
     qt[(4 * c4 + 1) * Cfg::kQPitch + row] = x.y;
     qt[(4 * c4 + 2) * Cfg::kQPitch + row] = x.z;
@@ -118,8 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key = idx % kBN;
       const int c4 = idx / kBN;
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + key < seq)
-        x = __ldg(reinterpret_cast<const float4*>(k + base + static_cast<size_t>(k0 + key) * D) + c4);
+      if (k0 + key < seq && 4 * c4 < hd)
+        x = __ldg(reinterpret_cast<const float4*>(k + base + static_cast<size_t>(k0 + key) * hd) + c4);
       kt[(4 * c4 + 0) * Cfg::kKPitch + key] = x.x;
       kt[(4 * c4 + 1) * Cfg::kKPitch + key] = x.y;
       kt[(4 * c4 + 2) * Cfg::kKPitch + key] = x.z;
@@ -129,8 +130,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int key = idx / (D / 4);
       const int c4 = idx % (D / 4);
       float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + key < seq)
-        x = __ldg(reinterpret_cast<const float4*>(v + base + static_cast<size_t>(k0 + key) * D) + c4);
+      if (k0 + key < seq && 4 * c4 < hd)
+        x = __ldg(reinterpret_cast<const float4*>(v + base + static_cast<size_t>(k0 + key) * hd) + c4);
       *reinterpret_cast<float4*>(&vs[key * Cfg::kVPitch + 4 * c4]) = x;
     }
     __syncthreads();
@@ -231,13 +232,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (row >= seq) continue;
       const size_t r_index = static_cast<size_t>(sp) * slice + static_cast<size_t>(bh) * seq + row;
       if (tc == 0) part_ml[r_index] = make_float2(m_run[i], l_run[i]);
-      float* orow = part_o + r_index * D + tc * Cfg::kCols;
+      float* orow = part_o + r_index * hd + tc * Cfg::kCols;
 #pragma unroll
       for (int c = 0; c < Cfg::kCols / 2; c += 2) {
         float a0, a1, b0, b1;
         unpack2f(o2[i][c], a0, a1);
         unpack2f(o2[i][c + 1], b0, b1);
-        *reinterpret_cast<float4*>(orow + 2 * c) = make_float4(a0, a1, b0, b1);
+        if (tc * Cfg::kCols + 2 * c < hd)
+          *reinterpret_cast<float4*>(orow + 2 * c) = make_float4(a0, a1, b0, b1);
       }
     }
     return;
@@ -247,13 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q0 + tr * 8 + i;
     if (row >= seq) continue;
     const float inv = 1.0f / l_run[i];
-    float* orow = out + base + static_cast<size_t>(row) * D + tc * Cfg::kCols;
+    float* orow = out + base + static_cast<size_t>(row) * hd + tc * Cfg::kCols;
 #pragma unroll
     for (int c = 0; c < Cfg::kCols / 2; c += 2) {
       float a0, a1, b0, b1;
       unpack2f(o2[i][c], a0, a1);
       unpack2f(o2[i][c + 1], b0, b1);
-      *reinterpret_cast<float4*>(orow + 2 * c) = make_float4(a0 * inv, a1 * inv, b0 * inv, b1 * inv);
+      if (tc * Cfg::kCols + 2 * c < hd)
+        *reinterpret_cast<float4*>(orow + 2 * c) =
+            make_float4(a0 * inv, a1 * inv, b0 * inv, b1 * inv);
     }
   }
 }
@@ -292,7 +296,7 @@ namespace {
 
 template <int D>
 cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, float* out,
-                             int heads_total, int seq, bool causal, cudaStream_t stream) {
+                             int heads_total, int seq, int hd, bool causal, cudaStream_t stream) {
   using Cfg = F32Cfg<D>;
   const size_t smem = Cfg::kSmemFloats * sizeof(float);
   cudaError_t e = cudaFuncSetAttribute(attention_f32_tiled_kernel<D>,
@@ -311,24 +315,24 @@ cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, flo
   }
   const long long ctas = units * splits;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
-  const float scale = 1.0f / sqrtf(static_cast<float>(D));
+  const float scale = 1.0f / sqrtf(static_cast<float>(hd));
   if (splits == 1) {
     attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
-        q, k, v, out, heads_total, seq, causal ? 1 : 0, scale, 1, nullptr, nullptr);
+        q, k, v, out, heads_total, seq, hd, causal ? 1 : 0, scale, 1, nullptr, nullptr);
     return cudaGetLastError();
   }
   const size_t rows = static_cast<size_t>(heads_total) * seq;
   void* ws = nullptr;
-  e = cudaMallocAsync(&ws, rows * splits * (D * sizeof(float) + sizeof(float2)), stream);
+  e = cudaMallocAsync(&ws, rows * splits * (hd * sizeof(float) + sizeof(float2)), stream);
   if (e != cudaSuccess) return e;
   float* part_o = static_cast<float*>(ws);
-  float2* part_ml = reinterpret_cast<float2*>(part_o + rows * splits * D);
+  float2* part_ml = reinterpret_cast<float2*>(part_o + rows * splits * hd);
   attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
-      q, k, v, out, heads_total, seq, causal ? 1 : 0, scale, splits, part_o, part_ml);
+      q, k, v, out, heads_total, seq, hd, causal ? 1 : 0, scale, splits, part_o, part_ml);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
     attention_combine_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
-        part_o, part_ml, out, rows, D, splits, 0);
+        part_o, part_ml, out, rows, hd, splits, 0);
     e = cudaGetLastError();
   }
   const cudaError_t f = cudaFreeAsync(ws, stream);
@@ -339,8 +343,9 @@ cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, flo
 
 bool attention_f32_tiled_supported(int head_dim, const void* q, const void* k, const void* v,
                                    const void* out) {
-  return (head_dim == 64 || head_dim == 128) && aligned16(q) && aligned16(k) &&
-         aligned16(v) && aligned16(out);
+  // Any head_dim <= 128 with float4 rows, computed as 64 or 128 (zero padding).
+  return head_dim >= 4 && head_dim <= 128 && head_dim % 4 == 0 && aligned16(q) &&
+         aligned16(k) && aligned16(v) && aligned16(out);
 }
 
 cudaError_t attention_f32_tiled(const float* q, const float* k, const float* v, float* out,
@@ -348,9 +353,11 @@ cudaError_t attention_f32_tiled(const float* q, const float* k, const float* v, 
                                 cudaStream_t stream) {
   const long long total = static_cast<long long>(batch) * heads;
   if (total > 0x7fffffffLL) return cudaErrorInvalidValue;
-  if (head_dim == 128)
-    return launch_f32_tiled<128>(q, k, v, out, static_cast<int>(total), seq, causal, stream);
-  return launch_f32_tiled<64>(q, k, v, out, static_cast<int>(total), seq, causal, stream);
+  if (head_dim > 64)
+    return launch_f32_tiled<128>(q, k, v, out, static_cast<int>(total), seq, head_dim, causal,
+                                 stream);
+  return launch_f32_tiled<64>(q, k, v, out, static_cast<int>(total), seq, head_dim, causal,
+                              stream);
 }
 
 }  // namespace opl

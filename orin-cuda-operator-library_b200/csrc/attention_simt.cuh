@@ -21,8 +21,9 @@ cudaError_t attention_f16_tc(const __half* q, const __half* k, const __half* v, 
                              int batch, int heads, int seq, int head_dim, bool causal,
                              cudaStream_t stream);
 
-// Tiled FP32 FFMA attention for head_dim 64 or 128 with 16-byte aligned
-// tensors (attention_f32_tiled_supported); other shapes use attention_simt.
+// Tiled FP32 FFMA attention for head_dim <= 128 with head_dim % 4 == 0
+// (computed as 64 or 128 with zero padding) and 16-byte aligned tensors
+// (attention_f32_tiled_supported); other shapes use attention_simt.
 bool attention_f32_tiled_supported(int head_dim, const void* q, const void* k, const void* v,
                                    const void* out);
 cudaError_t attention_f32_tiled(const float* q, const float* k, const float* v, float* out,
