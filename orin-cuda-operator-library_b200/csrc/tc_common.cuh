@@ -14,7 +14,6 @@ namespace tc {
 // Watchdog codes written when a bounded wait gives up.
 constexpr int kWatchdogGemm = 0x6e01;
 constexpr int kWatchdogAttention = 0x6e02;
-constexpr int kWatchdogRowCopy = 0x6e03;
 // Polls of mbarrier.try_wait (each may suspend the thread for a while) before
 // a wait is declared hung.  Far beyond any legitimate wait in these kernels.
 constexpr uint32_t kMaxPolls = 1u << 26;
@@ -94,17 +93,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Plain (untiled) bulk copy of `bytes` (multiple of 16, both addresses
-// 16-byte aligned) from global into shared memory, completing `bar`.
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
 
