@@ -321,11 +321,46 @@ __device__ __forceinline__ uint4 halves_at(const uint32_t (&w)[8], int o) {
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
+// Source words of a rows x cols FP16 matrix at any 2-byte-aligned base: the
+// 16-byte-aligned word holding the first element (inside the caller's
+// allocation, whose base is 256-byte aligned) and the element offset to it.
+struct HalfRows {
+  const uint4* src4;
+  size_t lead;          // halves before the first element in its word
+  size_t total_chunks;  // 16-byte words covering the matrix
+  int cols;
+  __device__ HalfRows(const __half* src, int rows, int cols_) : cols(cols_) {
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
+    lead = (addr & 15u) >> 1;
+    src4 = reinterpret_cast<const uint4*>(addr & ~uintptr_t(15));
+    total_chunks = (lead + static_cast<size_t>(rows) * cols + 7) / 8;
+  }
+  // Halves [8g, 8g + 8) of row r, zero past the row's end: built from the two
+  // aligned 16-byte words that cover them and a per-row byte shift, so all
+  // loads are 128-bit.
+  __device__ __forceinline__ uint4 group(int r, int g) const {
+    const size_t row_h = lead + static_cast<size_t>(r) * cols;
+    const size_t c0 = (row_h + static_cast<size_t>(g) * 8) >> 3;
+    const uint4 lo = __ldg(src4 + c0);
+    const uint4 hi = c0 + 1 < total_chunks ? __ldg(src4 + c0 + 1) : make_uint4(0, 0, 0, 0);
+    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    uint4 out = halves_at(w, static_cast<int>(row_h & 7));
+    const int valid = cols - g * 8;  // halves of this group inside the row
+    if (valid < 8) {
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (2 * i >= valid) ow[i] = 0;
+        else if (2 * i + 1 >= valid) ow[i] &= 0xffffu;
+      }
+    }
+    return out;
+  }
+};
+
 // Zero-padded copy of a rows x cols FP16 matrix (any 2-byte-aligned base,
 // any row stride) into a prow x pcol buffer (pcol a multiple of 8, so every row
-// starts 16-byte aligned for TMA).  Each output group of 8 halves is built
-// from the two aligned 16-byte source words that cover it and a byte shift
-// that is fixed per row, so all loads and stores are 128-bit.  With
+// starts 16-byte aligned for TMA), 128-bit loads and stores.  With
 // tail != nullptr it also gathers columns [tail_col0, tail_col0 + n_tail)
 // (n_tail <= blockDim.x) into the K-major strip tail[j][r] (row stride
 // tail_ld; zero for r >= rows).
@@ -335,40 +370,80 @@ __global__ void __launch_bounds__(256)
                     __half* __restrict__ tail = nullptr, int tail_col0 = 0, int n_tail = 0,
                     int tail_ld = 0) {
   const int groups = pcol / 8;
-  // Work from the 16-byte-aligned word holding the first element (inside
-  // the caller's allocation, whose base is 256-byte aligned).
-  const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
-  const size_t lead = (addr & 15u) >> 1;  // halves before src in its word
-  const uint4* src4 = reinterpret_cast<const uint4*>(addr & ~uintptr_t(15));
-  const size_t total_chunks = (lead + static_cast<size_t>(rows) * cols + 7) / 8;
+  const HalfRows in(src, rows, cols);
   for (int r = blockIdx.x; r < prow; r += gridDim.x) {
     uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
-    const size_t row_h = lead + static_cast<size_t>(r) * cols;
-    const int o = static_cast<int>(row_h & 7);
-    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
-      uint4 out = make_uint4(0, 0, 0, 0);
-      if (r < rows && g * 8 < cols) {
-        const size_t c0 = (row_h + static_cast<size_t>(g) * 8) >> 3;
-        const uint4 lo = __ldg(src4 + c0);
-        const uint4 hi = c0 + 1 < total_chunks ? __ldg(src4 + c0 + 1) : make_uint4(0, 0, 0, 0);
-        const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-        out = halves_at(w, o);
-        const int valid = cols - g * 8;  // halves of this group inside the row
-        if (valid < 8) {
-          uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if (2 * i >= valid) ow[i] = 0;
-            else if (2 * i + 1 >= valid) ow[i] &= 0xffffu;
-          }
-        }
-      }
-      drow[g] = out;
-    }
+    for (int g = threadIdx.x; g < groups; g += blockDim.x)
+      drow[g] = (r < rows && g * 8 < cols) ? in.group(r, g) : make_uint4(0, 0, 0, 0);
     if (tail != nullptr && static_cast<int>(threadIdx.x) < n_tail)
       tail[static_cast<size_t>(threadIdx.x) * tail_ld + r] =
           r < rows ? src[static_cast<size_t>(r) * cols + tail_col0 + threadIdx.x]
                    : __float2half(0.0f);
+  }
+}
+
+// Widest N remainder whose product the A-padding pass computes itself.
+constexpr int kPadDotMaxTail = 8;
+
+// pad_half_kernel for A (rows x cols into rows x pcol) that also computes the
+// narrow N remainder while each row is in registers: c[r][j] = sum over kk of
+// A[r][kk] * bt[j][kk] for j < n_tail <= kPadDotMaxTail, bt the K-major tail
+// strip of B (row stride pcol, zero past cols).  Products of two halves are
+// exact in FP32; each thread sums its groups in order, then warps and the
+// block in a fixed order, so results repeat bit for bit.  This replaces a
+// second full read of A by a skinny-N product after the GEMM.
+__global__ void __launch_bounds__(256)
+    pad_half_tail_dot_kernel(const __half* __restrict__ src, int rows, int cols,
+                             __half* __restrict__ dst, int pcol,
+                             const __half* __restrict__ bt, int n_tail,
+                             float* __restrict__ c, int ldc) {
+  __shared__ float part[8][kPadDotMaxTail];
+  const int groups = pcol / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const HalfRows in(src, rows, cols);
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
+    float acc[kPadDotMaxTail];
+#pragma unroll
+    for (int j = 0; j < kPadDotMaxTail; ++j) acc[j] = 0.0f;
+    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
+      const uint4 av = g * 8 < cols ? in.group(r, g) : make_uint4(0, 0, 0, 0);
+      drow[g] = av;
+      const __half2* a2 = reinterpret_cast<const __half2*>(&av);
+      float2 af[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) af[i] = __half22float2(a2[i]);
+#pragma unroll
+      for (int j = 0; j < kPadDotMaxTail; ++j) {
+        if (j < n_tail) {
+          const uint4 bv =
+              __ldg(reinterpret_cast<const uint4*>(bt + static_cast<size_t>(j) * pcol) + g);
+          const __half2* b2 = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 bf = __half22float2(b2[i]);
+            acc[j] = fmaf(af[i].x, bf.x, acc[j]);
+            acc[j] = fmaf(af[i].y, bf.y, acc[j]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kPadDotMaxTail; ++j) {
+      if (j < n_tail) {
+        float v = acc[j];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) part[warp][j] = v;
+      }
+    }
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < n_tail) {
+      float v = 0.0f;
+      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) v += part[w][threadIdx.x];
+      c[static_cast<size_t>(r) * ldc + threadIdx.x] = v;
+    }
+    __syncthreads();
   }
 }
 
@@ -691,8 +766,9 @@ __global__ void __launch_bounds__(256)
 // in a stream-ordered workspace.  When N ends in a narrow remainder (at most
 // 64 columns past a multiple of the 256-wide tile), the 256-wide kernel
 // covers the first n_main columns and the remainder runs as a skinny-N
-// product (gemm_small_n_tc) -- instead of one extra, almost empty tile per
-// 128 rows (4095 x 4097 x 4093: 544 tiles and a fourth wave vs 512 tiles).
+// product (gemm_small_n_tc, or, for at most 8 columns when A needs a padded
+// copy anyway, inside that copy's pass) -- instead of one extra, almost empty
+// tile per 128 rows (4095 x 4097 x 4093: 544 tiles and a fourth wave vs 512).
 cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n, int k,
                         cudaStream_t stream) {
   const bool a_ok = (k % 8 == 0) && aligned16(a);
@@ -717,11 +793,6 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
   uint8_t* wsb = static_cast<uint8_t*>(ws);
   const __half* a_use = a;
   const __half* b_use = b;
-  if (!a_ok) {
-    __half* dst = reinterpret_cast<__half*>(wsb);
-    pad_half_kernel<<<m < 65535 ? m : 65535, 256, 0, stream>>>(a, m, k, dst, m, kp);
-    a_use = dst;
-  }
   __half* bt = reinterpret_cast<__half*>(wsb + a_bytes + b_bytes);
   if (!b_ok) {  // (with a split, the same pass gathers the tail columns)
     __half* dst = reinterpret_cast<__half*>(wsb + a_bytes);
@@ -731,11 +802,24 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
   } else if (split_n) {
     tail_columns_kernel<<<(kp + 255) / 256, 256, 0, stream>>>(b, k, n, n_main, n_tail, bt, kp);
   }
+  // A narrow remainder is computed by the A-padding pass when there is one
+  // (after B's pass, which wrote the tail strip).
+  const bool tail_in_pad = split_n && !a_ok && n_tail <= kPadDotMaxTail;
+  if (!a_ok) {
+    __half* dst = reinterpret_cast<__half*>(wsb);
+    const int grid = m < 65535 ? m : 65535;
+    if (tail_in_pad)
+      pad_half_tail_dot_kernel<<<grid, 256, 0, stream>>>(a, m, k, dst, kp, bt, n_tail,
+                                                         c + n_main, n);
+    else
+      pad_half_kernel<<<grid, 256, 0, stream>>>(a, m, k, dst, m, kp);
+    a_use = dst;
+  }
   e = cudaGetLastError();
   const int lda = a_ok ? k : kp;
   const int ldb = b_ok ? n : ldb_copy;
   if (e == cudaSuccess) e = launch_gemm_tc(a_use, b_use, c, m, n_main, kp, lda, ldb, n, stream);
-  if (e == cudaSuccess && split_n)
+  if (e == cudaSuccess && split_n && !tail_in_pad)
     e = gemm_small_n_tc(a_use, lda, bt, kp, c + n_main, n, m, n_tail, kp, stream);
   const cudaError_t f = cudaFreeAsync(ws, stream);
   return e != cudaSuccess ? e : f;

@@ -48,7 +48,9 @@ GEMM_F16 = [(128, 128, 32), (16, 128, 32), (32, 32, 32), (37, 65, 71),  # ref te
             (4096, 4096, 4096), (300, 520, 136), (129, 257, 72),
             # narrow N remainders: 256-wide kernel + skinny-N tail product
             (1000, 4104, 512), (257, 300, 64), (200, 320, 96), (129, 513, 1000),
-            (640, 769, 333)]
+            (640, 769, 333),
+            # ragged K with a remainder of <= 8 columns: computed in A's padding pass
+            (300, 262, 77), (200, 520, 45), (1000, 1033, 999)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_F16)
