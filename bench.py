@@ -445,7 +445,12 @@ def bench_rowops(args, dist, dev, peaks):
 # ------------------------------------------------------------ other configs
 
 def _rotations(bytes_per_set: int) -> int:
-    return max(1, min(8, -(-2 * L2_BYTES // max(bytes_per_set, 1)) + 1))
+    """Input sets to rotate through: together at least 2x L2 plus one set,
+    at most 2 GiB.  Launch i reads set i % sets, so with at least as many
+    launches per graph as sets, a set is read again only after 2x L2 of
+    other inputs."""
+    b = max(bytes_per_set, 1)
+    return max(1, min(-(-2 * L2_BYTES // b) + 1, (2 << 30) // b))
 
 
 def _measure(call, steps, warmup, dist, stream, graph=True):
@@ -474,7 +479,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
     stream = torch.cuda.current_stream(dev)
     h = stream.cuda_stream
     rng = np.random.default_rng(77 + dist.rank)
-    steps = max(3, min(args.steps, 20))
+    steps = max(3, min(args.steps, 40))  # launches per graph: >= the rotation sets
     warm = max(3, min(args.warmup, 5))
     hbm = peaks["hbm_gbs"]
     tc = peaks["bf16_tflops"]
@@ -484,11 +489,13 @@ def extras(args, dist, dev, peaks, only: set[str]):
     def want(name):
         return not only or name in only
 
-    def record(name, ms, work, bound, peak, unit, note=None, world_units=1):
+    def record(name, ms, work, bound, peak, unit, note=None, world_units=1, sets=None):
         scale = 1e9 if unit == "GB/s" else 1e12
         rate = work * world_units / (ms * 1e-3) / scale
         r = {"ms": round(ms, 5), "value": round(rate, 3), "unit": unit,
              "bound": bound, "frac_per_gpu": round(rate / world_units / peak, 4)}
+        if sets is not None:  # (input sets, bytes of one set)
+            r["inputs"] = f"{sets[0]} rotating sets, {sets[0] * sets[1] / 2**20:.0f} MiB"
         if note:
             r["note"] = note
         out[name] = r
@@ -529,28 +536,29 @@ def extras(args, dist, dev, peaks, only: set[str]):
             record("reduce_16M_nccl", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world,
                    note="per-GPU FP64 partial + NCCL all-reduce (comparison)")
         else:
-            record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s")
+            record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", sets=(len(xs), 4 * n))
 
     # ragged row ops 4097x1023
     if want("ragged"):
         r, c = 4097, 1023
-        x = [t(rng.normal(0, 2, (r, c)).astype(np.float32)) for _ in range(_rotations(8 * r * c))]
+        x = [t(rng.normal(0, 2, (r, c)).astype(np.float32)) for _ in range(_rotations(4 * r * c))]
+        rs = (len(x), 4 * r * c)
         y = torch.empty((r, c), device=dev)
         yt = torch.empty((c, r), device=dev)
         w = t(rng.normal(1, 0.1, c).astype(np.float32))
         ms = _measure(lambda i, h: lib.opl_softmax_f32(x[i % len(x)].data_ptr(), y.data_ptr(), r, c, h), steps, warm, dist, stream)
-        record("softmax_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
+        record("softmax_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world, sets=rs)
         ms = _measure(lambda i, h: lib.opl_rmsnorm_f32(x[i % len(x)].data_ptr(), w.data_ptr(), y.data_ptr(), r, c, RMS_EPS, h), steps, warm, dist, stream)
-        record("rmsnorm_4097x1023", ms, 8 * r * c + 4 * c, "hbm", hbm, "GB/s", world_units=dist.world)
+        record("rmsnorm_4097x1023", ms, 8 * r * c + 4 * c, "hbm", hbm, "GB/s", world_units=dist.world, sets=rs)
         ms = _measure(lambda i, h: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
-        record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world)
+        record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world, sets=rs)
 
     # 16-bit I/O row ops: BF16 softmax 4096x1024, RMSNorm 2048x4096
     if want("row16"):
         for tag, fn, (r, c) in [("softmax_bf16_4096x1024", lib.opl_softmax_bf16, SOFTMAX_SHAPE),
                                 ("rmsnorm_bf16_2048x4096", lib.opl_rmsnorm_bf16, RMS_SHAPE)]:
             xs16 = [t(rng.normal(0, 1, (r, c)).astype(np.float32)).to(torch.bfloat16)
-                    for _ in range(_rotations(4 * r * c))]
+                    for _ in range(_rotations(2 * r * c))]
             w16 = t(rng.normal(1, 0.1, c).astype(np.float32)).to(torch.bfloat16)
             y16 = torch.empty((r, c), device=dev, dtype=torch.bfloat16)
             if tag.startswith("softmax"):
@@ -561,7 +569,8 @@ def extras(args, dist, dev, peaks, only: set[str]):
                                           y16.data_ptr(), r, c, RMS_EPS, hh)
                 work = 4 * r * c + 2 * c
             ms = _measure(call16, steps, warm, dist, stream)
-            record(tag, ms, work, "hbm", hbm, "GB/s", world_units=dist.world)
+            record(tag, ms, work, "hbm", hbm, "GB/s", world_units=dist.world,
+                   sets=(len(xs16), 2 * r * c))
             del xs16
 
     # GEMM 4096^3 FP16 (tensor cores), FP32 (FFMA), non-aligned FP16
@@ -570,15 +579,19 @@ def extras(args, dist, dev, peaks, only: set[str]):
                                    ("gemm_f32_4096", np.float32, (4096, 4096, 4096))]:
         if not want(name.rsplit("_", 1)[0]) and not want(name):
             continue
-        a = t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dtype))
-        b = t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype))
+        set_bytes = np.dtype(dtype).itemsize * (m * k + k * n)
+        ab = [(t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dtype)),
+               t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype)))
+              for _ in range(_rotations(set_bytes))]
         cc = torch.empty((m, n), device=dev)
         fn = lib.opl_gemm_f16 if dtype == np.float16 else lib.opl_gemm_f32
-        ms = _measure(lambda i, h: fn(a.data_ptr(), b.data_ptr(), cc.data_ptr(), m, n, k, h),
+        ms = _measure(lambda i, h: fn(ab[i % len(ab)][0].data_ptr(), ab[i % len(ab)][1].data_ptr(),
+                                      cc.data_ptr(), m, n, k, h),
                       max(3, steps // 2), warm, dist, stream)
         peak = tc if dtype == np.float16 else ffma
         record(name, ms, 2.0 * m * n * k, "tensor" if dtype == np.float16 else "ffma",
-               peak, "TFLOP/s", world_units=dist.world)
+               peak, "TFLOP/s", world_units=dist.world, sets=(len(ab), set_bytes))
+        del ab
 
     # skinny FP16 GEMM (decode shapes):
     # bound by streaming B, reported as GB/s of A + B + C
@@ -594,7 +607,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
                           steps, warm, dist, stream)
             record(f"gemm_f16_m{m}_4096x4096", ms, 2 * (m * k + k * n) + 4 * m * n, "hbm", hbm,
                    "GB/s", note=f"{2.0 * m * n * k / (ms * 1e-3) / 1e12:.2f} TFLOP/s",
-                   world_units=dist.world)
+                   world_units=dist.world, sets=(len(bs), 2 * k * n))
         del bs
 
     # attention B1 H12 S1024 D128, FP16 and FP32, causal and not
@@ -603,17 +616,20 @@ def extras(args, dist, dev, peaks, only: set[str]):
         if not want(f"attention_{tag}"):
             continue
         shape = (1, 12, 1024, 128)
-        q, k_, v = (t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+        set_bytes = 3 * np.dtype(dtype).itemsize * int(np.prod(shape))
+        qkv = [tuple(t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+               for _ in range(_rotations(set_bytes))]
         o = torch.empty(shape, device=dev)
         fn = lib.opl_attention_f16 if tag == "f16" else lib.opl_attention_f32
         for causal in (0, 1):
-            ms = _measure(lambda i, h: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(),
+            ms = _measure(lambda i, h: fn(*(x.data_ptr() for x in qkv[i % len(qkv)]), o.data_ptr(),
                                        1, 12, 1024, 128, causal, h), steps, warm, dist, stream)
             flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
             record(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops,
                    "tensor" if tag == "f16" else "ffma", tc if tag == "f16" else ffma,
                    "TFLOP/s", note="causal-exact FLOPs" if causal else None,
-                   world_units=dist.world)
+                   world_units=dist.world, sets=(len(qkv), set_bytes))
+        del qkv
 
     # sharded causal attention B8 H32 S4096 D128 (strong scaling over B*H)
     if want("attn_sharded"):
@@ -695,18 +711,19 @@ def ref_b200(args, dist, dev, peaks):
     del xs
     for dtype, fn, tag in [(np.float16, ref.ref_gemm_f16, "gemm_f16_4096"),
                            (np.float32, ref.ref_gemm_f32, "gemm_f32_4096")]:
-        a = t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype))
-        b = t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype))
+        ab = [tuple(t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype)) for _ in range(2))
+              for _ in range(_rotations(2 * np.dtype(dtype).itemsize * 4096 * 4096))]
         c = torch.empty((4096, 4096), device=dev)
-        ms = _measure(lambda i, h: fn(a.data_ptr(), b.data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), 3, 1, dist, stream)
+        ms = _measure(lambda i, h: fn(ab[i % len(ab)][0].data_ptr(), ab[i % len(ab)][1].data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), 3, 1, dist, stream)
         rate(tag, ms, 2.0 * 4096**3, "TFLOP/s")
     shape = (1, 12, 1024, 128)
     for dtype, fn, tag in [(np.float16, ref.ref_attention_f16, "f16"),
                            (np.float32, ref.ref_attention_f32, "f32")]:
-        q, k_, v = (t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+        qkv = [tuple(t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+               for _ in range(_rotations(3 * np.dtype(dtype).itemsize * int(np.prod(shape))))]
         o = torch.empty(shape, device=dev)
         for causal in (0, 1):
-            ms = _measure(lambda i, h: fn(q.data_ptr(), k_.data_ptr(), v.data_ptr(), o.data_ptr(), 1, 12, 1024, 128, causal, h), 3, 1, dist, stream)
+            ms = _measure(lambda i, h: fn(*(x.data_ptr() for x in qkv[i % len(qkv)]), o.data_ptr(), 1, 12, 1024, 128, causal, h), 3, 1, dist, stream)
             flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
             rate(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops, "TFLOP/s")
     torch.cuda.empty_cache()
