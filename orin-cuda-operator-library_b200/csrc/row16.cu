@@ -28,6 +28,17 @@ struct Io16<__nv_bfloat16> {
   static __device__ __forceinline__ __nv_bfloat16 store(float f) { return __float2bfloat16_rn(f); }
 };
 
+// e^x as 2^(x log2 e) on the MUFU ex2 unit (ex2.approx.f32, relative error
+// about 2^-22; subnormal results kept).  With x = v - m formed first, the
+// argument's rounding adds at most ~1e-5 relative for |x| < 88, far below the
+// rounding of the 16-bit output (2^-11 for FP16, 2^-8 for BF16), where
+// CUDA's expf spends several FMA and ALU instructions per element.
+__device__ __forceinline__ float exp_mufu(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x * 1.4426950408889634f));
+  return y;
+}
+
 template <typename T, int kGroup, int kItems, bool kVec>
 __device__ __forceinline__ void load16(const T* __restrict__ row, int cols, int t, float fill,
                                        float (&v)[kItems * (kVec ? 8 : 1)]) {
@@ -101,7 +112,7 @@ __global__ void __launch_bounds__(kBlock)
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < kItems * kW; ++i) {
-    v[i] = expf(v[i] - m);
+    v[i] = exp_mufu(v[i] - m);  // padding slots (-FLT_MAX) underflow to 0
     s += v[i];
   }
   s = group_reduce<kGroup, kBlock, false>(s, scratch_sum);
