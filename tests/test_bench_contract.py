@@ -30,3 +30,17 @@ def test_reference_arm_prints_one_contract_line():
     import bench
 
     assert d["config"]["workload"] == bench.WORKLOAD  # same config as the GPU arm
+
+
+def test_rotation_sets_exceed_twice_l2():
+    """Timed inputs rotate over sets that together exceed 2x L2 (plus one set),
+    within 2 GiB; sets larger than L2 need no rotation beyond that rule."""
+    import bench
+
+    for set_bytes in [1 << 20, 8_388_608, 16_764_924, 33_554_432, 67_108_864,
+                      134_217_728, 1 << 30, 3 << 30]:
+        sets = bench._rotations(set_bytes)
+        assert sets >= 1
+        assert sets * set_bytes <= max(2 << 30, set_bytes)
+        if (2 << 30) // set_bytes > -(-2 * bench.L2_BYTES // set_bytes):
+            assert (sets - 1) * set_bytes >= 2 * bench.L2_BYTES
