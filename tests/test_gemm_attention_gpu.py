@@ -198,22 +198,26 @@ def test_attention_f16_paired_tiles_sampled_heads(cuda, stream, b, h, s, d, caus
     check_f16(got[idx], want)
 
 
-@pytest.mark.parametrize("m,n,k,offset", [(64, 72, 40, 1), (300, 200, 136, 3), (129, 257, 72, 5),
-                                          (1000, 1000, 1000, 7)])
-def test_gemm_f16_misaligned_base_pointers(cuda, stream, m, n, k, offset):
-    """A and B start `offset` halves into their allocations (2-byte aligned
-    only): the zero-padded staging path must read them correctly."""
+@pytest.mark.parametrize("m,n,k,offset,b_offset", [
+    (64, 72, 40, 1, 1), (300, 200, 136, 3, 3), (129, 257, 72, 5, 5), (1000, 1000, 1000, 7, 7),
+    # only A misaligned, N a multiple of 256 plus <= 8: B stays in place and
+    # the remainder columns are computed in A's padding pass
+    (300, 264, 64, 3, 0), (129, 520, 136, 1, 0)])
+def test_gemm_f16_misaligned_base_pointers(cuda, stream, m, n, k, offset, b_offset):
+    """A starts `offset` halves and B `b_offset` halves into their allocations
+    (2-byte aligned only): the zero-padded staging path must read them
+    correctly."""
     import torch
 
     rng = np.random.default_rng(m + offset)
     a = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float16)
     b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16)
     a_full = torch.zeros(m * k + offset, dtype=torch.float16, device=cuda)
-    b_full = torch.zeros(k * n + offset, dtype=torch.float16, device=cuda)
+    b_full = torch.zeros(k * n + b_offset, dtype=torch.float16, device=cuda)
     a_full[offset:] = torch.from_numpy(a.ravel()).to(cuda)
-    b_full[offset:] = torch.from_numpy(b.ravel()).to(cuda)
+    b_full[b_offset:] = torch.from_numpy(b.ravel()).to(cuda)
     c = torch.empty((m, n), device=cuda)
-    operatorlib.gemm_into(a_full[offset:].view(m, k), b_full[offset:].view(k, n), c)
+    operatorlib.gemm_into(a_full[offset:].view(m, k), b_full[b_offset:].view(k, n), c)
     stream.synchronize()
     check_f16(c.cpu().numpy(), orc.gemm(a.astype(np.float32), b.astype(np.float32), threads=8))
 
