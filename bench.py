@@ -714,7 +714,7 @@ def ref_b200(args, dist, dev, peaks):
         ab = [tuple(t((rng.uniform(-1, 1, (4096, 4096)) / 64).astype(dtype)) for _ in range(2))
               for _ in range(_rotations(2 * np.dtype(dtype).itemsize * 4096 * 4096))]
         c = torch.empty((4096, 4096), device=dev)
-        ms = _measure(lambda i, h: fn(ab[i % len(ab)][0].data_ptr(), ab[i % len(ab)][1].data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), 3, 1, dist, stream)
+        ms = _measure(lambda i, h: fn(ab[i % len(ab)][0].data_ptr(), ab[i % len(ab)][1].data_ptr(), c.data_ptr(), 4096, 4096, 4096, h), max(3, len(ab)), 1, dist, stream)
         rate(tag, ms, 2.0 * 4096**3, "TFLOP/s")
     shape = (1, 12, 1024, 128)
     for dtype, fn, tag in [(np.float16, ref.ref_attention_f16, "f16"),
@@ -723,7 +723,7 @@ def ref_b200(args, dist, dev, peaks):
                for _ in range(_rotations(3 * np.dtype(dtype).itemsize * int(np.prod(shape))))]
         o = torch.empty(shape, device=dev)
         for causal in (0, 1):
-            ms = _measure(lambda i, h: fn(*(x.data_ptr() for x in qkv[i % len(qkv)]), o.data_ptr(), 1, 12, 1024, 128, causal, h), 3, 1, dist, stream)
+            ms = _measure(lambda i, h: fn(*(x.data_ptr() for x in qkv[i % len(qkv)]), o.data_ptr(), 1, 12, 1024, 128, causal, h), max(3, len(qkv)), 1, dist, stream)
             flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
             rate(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops, "TFLOP/s")
     torch.cuda.empty_cache()
