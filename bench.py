@@ -44,6 +44,7 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 L2_BYTES = 126 * 2**20
+FFMA_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # FP32 FFMA spec peak, TFLOP/s
 
 SOFTMAX_SHAPE = (4096, 1024)
 RMS_SHAPE = (2048, 4096)
@@ -72,6 +73,10 @@ def parse_args(argv=None):
                         "gemm_f32|attention_f16|attention_f32)")
     p.add_argument("--shape", default="",
                    help="shape for --profile, e.g. 4096,4096,4096 or 1,12,1024,128,1")
+    p.add_argument("--sets", type=int, default=1,
+                   help="--profile: rotate row-op / reduce launches over this many "
+                        "input+output buffer sets (DRAM traffic per launch with "
+                        "write-backs of earlier launches counted)")
     p.add_argument("--only", default="",
                    help="comma list of extra workloads to run (default all)")
     return p.parse_args(argv)
@@ -129,6 +134,21 @@ class Dist:
         t = torch.tensor([value], dtype=torch.float64, device=dev)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
+
+    def sum(self, value: float) -> float:
+        """FP64 sum of `value` over ranks (identity at one rank)."""
+        if self.pg is None:
+            return value
+        import torch
+
+        dev = "cuda" if torch.cuda.is_available() else "cpu"
+        t = torch.tensor([value], dtype=torch.float64, device=dev)
+        self.pg.all_reduce(t)
+        return float(t.item())
+
+    def all_true(self, flag: bool) -> bool:
+        """True when `flag` holds on every rank."""
+        return self.sum(0.0 if flag else 1.0) == 0.0
 
     def close(self):
         if self.pg is not None:
@@ -467,13 +487,28 @@ def _measure(call, steps, warmup, dist, stream, graph=True):
     return graph_ms_per_launch(lambda i, h: checked(i, h), steps, max(3, warmup), dist, stream)
 
 
+def _f16_gate(got, want) -> tuple[bool, float]:
+    """North-star FP16 gate (max abs <= 2e-2, |err| <= 2e-2 |ref| + 2e-2,
+    Frobenius-relative <= 1e-2) against an FP64/FP32 oracle; (ok, max abs)."""
+    got = np.asarray(got, dtype=np.float64)
+    err = np.abs(got - want)
+    fro = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+    ok = bool(err.max() <= 2e-2 and np.all(err <= 2e-2 * np.abs(want) + 2e-2) and fro <= 1e-2)
+    return ok, float(err.max())
+
+
 def extras(args, dist, dev, peaks, only: set[str]):
-    """Every BASELINE config besides the headline; returns {name: record}.
-    Row ops / reduce: weak-scaled per rank.  'attn_sharded' and
-    'gemm_sharded': strong-scaled, units split contiguously across ranks."""
+    """Every BASELINE config besides the headline.  Returns (records,
+    parity): records[name] = {"ms", "value", "unit", "frac", "sets"?};
+    parity[name] = [ok, max error] from a check of this rank's own output
+    against the CPU oracle (sampled rows / heads for the large shapes), made
+    outside the timed region.  Row ops / reduce: weak-scaled per rank.
+    'attn_sharded' and 'gemm_sharded': strong-scaled, units split
+    contiguously across ranks."""
     import torch
 
     import operatorlib
+    from oracle import oracle as orc
 
     lib = operatorlib.capi()
     stream = torch.cuda.current_stream(dev)
@@ -483,48 +518,63 @@ def extras(args, dist, dev, peaks, only: set[str]):
     warm = max(3, min(args.warmup, 5))
     hbm = peaks["hbm_gbs"]
     tc = peaks["bf16_tflops"]
-    ffma = 148 * 128 * 2 * 1.965e9 / 1e12  # FP32 FFMA spec peak, TFLOP/s
-    out = {}
+    ffma = FFMA_TFLOPS
+    out, parity = {}, {}
 
     def want(name):
         return not only or name in only
 
-    def record(name, ms, work, bound, peak, unit, note=None, world_units=1, sets=None):
+    def record(name, ms, work, peak, unit, world_units=1, sets=None, **extra):
         scale = 1e9 if unit == "GB/s" else 1e12
         rate = work * world_units / (ms * 1e-3) / scale
-        r = {"ms": round(ms, 5), "value": round(rate, 3), "unit": unit,
-             "bound": bound, "frac_per_gpu": round(rate / world_units / peak, 4)}
+        r = {"ms": round(ms, 5), "value": round(rate, 2), "unit": unit,
+             "frac": round(rate / world_units / peak, 4)}
         if sets is not None:  # (input sets, bytes of one set)
-            r["inputs"] = f"{sets[0]} rotating sets, {sets[0] * sets[1] / 2**20:.0f} MiB"
-        if note:
-            r["note"] = note
+            r["sets"] = [sets[0], round(sets[0] * sets[1] / 2**20)]
+        r.update(extra)
         out[name] = r
 
     def t(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 
+    def sync_host(x):
+        torch.cuda.synchronize()
+        return x.cpu().numpy()
+
     # reduce: N = 16,777,216 per rank (weak); partial in FP64 + NCCL all-reduce
     if want("reduce"):
         n = 16_777_216
-        xs = [t(rng.uniform(-1, 1, n).astype(np.float32)) for _ in range(_rotations(4 * n))]
+        x0 = rng.uniform(-1, 1, n).astype(np.float32)
+        xs = [t(x0)] + [t(rng.uniform(-1, 1, n).astype(np.float32))
+                        for _ in range(_rotations(4 * n) - 1)]
         part = torch.empty((), dtype=torch.float64, device=dev)
         res = torch.empty((), device=dev)
 
         if dist.world == 1:
             ms = _measure(lambda i, hh: lib.opl_reduce_sum_f32(xs[i % len(xs)].data_ptr(), res.data_ptr(), n, hh),
                           steps, warm, dist, stream)
+            record("reduce_16M", ms, 4 * n, hbm, "GB/s", sets=(len(xs), 4 * n))
+            lib.opl_reduce_sum_f32(xs[0].data_ptr(), res.data_ptr(), n, h)
+            want_sum = orc.reduce_sum(x0)
+            got = float(sync_host(res))
+            err = abs(got - want_sum) / max(abs(want_sum), 1e-30)
+            parity["reduce_16M"] = [bool(err <= 1e-6), float(f"{err:.2e}")]
         else:
             # Fused: partial sums exchanged over NVLink peer memory inside the
             # reduce's finalize kernel (operatorlib.ReduceTeam).
-            import operatorlib as _ol
-
-            team = _ol.ReduceTeam(dist.rank, dist.world)
+            team = operatorlib.ReduceTeam(dist.rank, dist.world)
             ms = _measure(lambda i, hh: team.launch(xs[i % len(xs)], res, hh), steps, warm,
                           dist, stream)
-            record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world,
-                   note="fused: per-GPU FP64 partial + all-reduce over NVLink peer stores")
+            record("reduce_16M", ms, 4 * n, hbm, "GB/s", world_units=dist.world)
+            # every rank must hold the same total: the FP64 sum of all chunks
+            team.launch(xs[0], res, h)
+            got = float(sync_host(res))
+            want_sum = dist.sum(orc.reduce_sum(x0))
+            err = abs(got - want_sum) / max(abs(want_sum), 1e-30)
+            parity["reduce_16M"] = [bool(err <= 1e-6), float(f"{err:.2e}")]
             team.close()
-        if dist.world > 1:  # local FP64 partial + NCCL FP64 all-reduce, captured together
+
+            # local FP64 partial + NCCL FP64 all-reduce, captured together
             def call(i, hh):
                 rc = lib.opl_reduce_sum_partial_f64(xs[i % len(xs)].data_ptr(), part.data_ptr(), n, hh)
                 dist.pg.all_reduce(part)
@@ -533,25 +583,40 @@ def extras(args, dist, dev, peaks, only: set[str]):
                 ms = _measure(call, steps, warm, dist, stream)
             except Exception:  # NCCL without graph-capture support: eager launches
                 ms = _measure(lambda i: call(i, h), steps, warm, dist, stream, graph=False)
-            record("reduce_16M_nccl", ms, 4 * n, "hbm", hbm, "GB/s", world_units=dist.world,
-                   note="per-GPU FP64 partial + NCCL all-reduce (comparison)")
-        else:
-            record("reduce_16M", ms, 4 * n, "hbm", hbm, "GB/s", sets=(len(xs), 4 * n))
+            record("reduce_16M_nccl", ms, 4 * n, hbm, "GB/s", world_units=dist.world)
+        del xs
 
     # ragged row ops 4097x1023
     if want("ragged"):
         r, c = 4097, 1023
-        x = [t(rng.normal(0, 2, (r, c)).astype(np.float32)) for _ in range(_rotations(4 * r * c))]
+        x0 = rng.normal(0, 2, (r, c)).astype(np.float32)
+        x = [t(x0)] + [t(rng.normal(0, 2, (r, c)).astype(np.float32))
+                       for _ in range(_rotations(4 * r * c) - 1)]
         rs = (len(x), 4 * r * c)
         y = torch.empty((r, c), device=dev)
         yt = torch.empty((c, r), device=dev)
-        w = t(rng.normal(1, 0.1, c).astype(np.float32))
+        w0 = rng.normal(1, 0.1, c).astype(np.float32)
+        w = t(w0)
         ms = _measure(lambda i, h: lib.opl_softmax_f32(x[i % len(x)].data_ptr(), y.data_ptr(), r, c, h), steps, warm, dist, stream)
-        record("softmax_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world, sets=rs)
+        record("softmax_4097x1023", ms, 8 * r * c, hbm, "GB/s", world_units=dist.world, sets=rs)
+        lib.opl_softmax_f32(x[0].data_ptr(), y.data_ptr(), r, c, h)
+        ref = orc.softmax(x0)
+        err = np.abs(sync_host(y) - ref)
+        parity["softmax_4097x1023"] = [bool(np.all(err <= 1e-5 * np.abs(ref) + 1e-7)),
+                                       float(f"{err.max():.2e}")]
         ms = _measure(lambda i, h: lib.opl_rmsnorm_f32(x[i % len(x)].data_ptr(), w.data_ptr(), y.data_ptr(), r, c, RMS_EPS, h), steps, warm, dist, stream)
-        record("rmsnorm_4097x1023", ms, 8 * r * c + 4 * c, "hbm", hbm, "GB/s", world_units=dist.world, sets=rs)
+        record("rmsnorm_4097x1023", ms, 8 * r * c + 4 * c, hbm, "GB/s", world_units=dist.world, sets=rs)
+        lib.opl_rmsnorm_f32(x[0].data_ptr(), w.data_ptr(), y.data_ptr(), r, c, RMS_EPS, h)
+        ref = orc.rmsnorm(x0, w0, RMS_EPS)
+        err = np.abs(sync_host(y) - ref)
+        parity["rmsnorm_4097x1023"] = [bool(np.all(err <= 1e-5 * np.abs(ref) + 1e-7)),
+                                       float(f"{err.max():.2e}")]
         ms = _measure(lambda i, h: lib.opl_transpose_f32(x[i % len(x)].data_ptr(), yt.data_ptr(), r, c, h), steps, warm, dist, stream)
-        record("transpose_4097x1023", ms, 8 * r * c, "hbm", hbm, "GB/s", world_units=dist.world, sets=rs)
+        record("transpose_4097x1023", ms, 8 * r * c, hbm, "GB/s", world_units=dist.world, sets=rs)
+        lib.opl_transpose_f32(x[0].data_ptr(), yt.data_ptr(), r, c, h)
+        parity["transpose_4097x1023"] = [
+            bool(np.array_equal(sync_host(yt).view(np.uint32), orc.transpose(x0).view(np.uint32))), 0.0]
+        del x
 
     # 16-bit I/O row ops: BF16 softmax 4096x1024, RMSNorm 2048x4096
     if want("row16"):
@@ -569,8 +634,16 @@ def extras(args, dist, dev, peaks, only: set[str]):
                                           y16.data_ptr(), r, c, RMS_EPS, hh)
                 work = 4 * r * c + 2 * c
             ms = _measure(call16, steps, warm, dist, stream)
-            record(tag, ms, work, "hbm", hbm, "GB/s", world_units=dist.world,
+            record(tag, ms, work, hbm, "GB/s", world_units=dist.world,
                    sets=(len(xs16), 2 * r * c))
+            # one BF16 rounding of the FP32-exact result: within 1 ulp (2^-8 rel)
+            call16(0, h)
+            x32 = sync_host(xs16[0].float())
+            ref = (orc.softmax(x32) if tag.startswith("softmax")
+                   else orc.rmsnorm(x32, sync_host(w16.float()), RMS_EPS))
+            err = np.abs(sync_host(y16.float()) - ref)
+            parity[tag] = [bool(np.all(err <= 2.0**-8 * np.abs(ref) + 1e-30)),
+                           float(f"{err.max():.2e}")]
             del xs16
 
     # GEMM 4096^3 FP16 (tensor cores), FP32 (FFMA), non-aligned FP16
@@ -580,17 +653,29 @@ def extras(args, dist, dev, peaks, only: set[str]):
         if not want(name.rsplit("_", 1)[0]) and not want(name):
             continue
         set_bytes = np.dtype(dtype).itemsize * (m * k + k * n)
-        ab = [(t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dtype)),
-               t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype)))
-              for _ in range(_rotations(set_bytes))]
+        a0 = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dtype)
+        b0 = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype)
+        ab = [(t(a0), t(b0))] + [(t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(dtype)),
+                                  t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(dtype)))
+                                 for _ in range(_rotations(set_bytes) - 1)]
         cc = torch.empty((m, n), device=dev)
         fn = lib.opl_gemm_f16 if dtype == np.float16 else lib.opl_gemm_f32
         ms = _measure(lambda i, h: fn(ab[i % len(ab)][0].data_ptr(), ab[i % len(ab)][1].data_ptr(),
                                       cc.data_ptr(), m, n, k, h),
                       max(3, steps // 2), warm, dist, stream)
         peak = tc if dtype == np.float16 else ffma
-        record(name, ms, 2.0 * m * n * k, "tensor" if dtype == np.float16 else "ffma",
-               peak, "TFLOP/s", world_units=dist.world, sets=(len(ab), set_bytes))
+        record(name, ms, 2.0 * m * n * k, peak, "TFLOP/s", world_units=dist.world,
+               sets=(len(ab), set_bytes))
+        fn(ab[0][0].data_ptr(), ab[0][1].data_ptr(), cc.data_ptr(), m, n, k, h)
+        idx = np.unique(np.linspace(0, m - 1, 32).astype(int))
+        got = sync_host(cc[torch.from_numpy(idx).to(dev)])
+        ref = a0[idx].astype(np.float64) @ b0.astype(np.float64)
+        if dtype == np.float16:
+            ok, e = _f16_gate(got, ref)
+        else:  # the reference's FP32 GEMM gate (tests/gemm_smoke.cu:76)
+            e = float(np.abs(got - ref).max())
+            ok = bool(np.all(np.abs(got - ref) <= 1e-3 + 1e-3 * np.abs(ref)))
+        parity[name] = [ok, float(f"{e:.2e}")]
         del ab
 
     # skinny FP16 GEMM (decode shapes):
@@ -598,17 +683,23 @@ def extras(args, dist, dev, peaks, only: set[str]):
     if want("gemv"):
         for m in (1, 16):
             n = k = 4096
-            a = t((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float16))
-            bs = [t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16))
-                  for _ in range(_rotations(2 * k * n))]
+            a0 = (rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float16)
+            b0 = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16)
+            a = t(a0)
+            bs = [t(b0)] + [t((rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float16))
+                            for _ in range(_rotations(2 * k * n) - 1)]
             cc = torch.empty((m, n), device=dev)
             ms = _measure(lambda i, h: lib.opl_gemm_f16(a.data_ptr(), bs[i % len(bs)].data_ptr(),
                                                         cc.data_ptr(), m, n, k, h),
                           steps, warm, dist, stream)
-            record(f"gemm_f16_m{m}_4096x4096", ms, 2 * (m * k + k * n) + 4 * m * n, "hbm", hbm,
-                   "GB/s", note=f"{2.0 * m * n * k / (ms * 1e-3) / 1e12:.2f} TFLOP/s",
-                   world_units=dist.world, sets=(len(bs), 2 * k * n))
-        del bs
+            name = f"gemm_f16_m{m}_4096x4096"
+            record(name, ms, 2 * (m * k + k * n) + 4 * m * n, hbm,
+                   "GB/s", world_units=dist.world, sets=(len(bs), 2 * k * n),
+                   tflops=round(2.0 * m * n * k / (ms * 1e-3) / 1e12, 2))
+            lib.opl_gemm_f16(a.data_ptr(), bs[0].data_ptr(), cc.data_ptr(), m, n, k, h)
+            parity[name] = [*_f16_gate(sync_host(cc), a0.astype(np.float64) @ b0.astype(np.float64))]
+            parity[name][1] = float(f"{parity[name][1]:.2e}")
+            del bs
 
     # attention B1 H12 S1024 D128, FP16 and FP32, causal and not
     for dtype in (np.float16, np.float32):
@@ -617,18 +708,35 @@ def extras(args, dist, dev, peaks, only: set[str]):
             continue
         shape = (1, 12, 1024, 128)
         set_bytes = 3 * np.dtype(dtype).itemsize * int(np.prod(shape))
-        qkv = [tuple(t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
-               for _ in range(_rotations(set_bytes))]
+        qkv0 = [rng.normal(0, 1, shape).astype(dtype) for _ in range(3)]
+        qkv = [tuple(t(x) for x in qkv0)] + [
+            tuple(t(rng.normal(0, 1, shape).astype(dtype)) for _ in range(3))
+            for _ in range(_rotations(set_bytes) - 1)]
         o = torch.empty(shape, device=dev)
         fn = lib.opl_attention_f16 if tag == "f16" else lib.opl_attention_f32
         for causal in (0, 1):
             ms = _measure(lambda i, h: fn(*(x.data_ptr() for x in qkv[i % len(qkv)]), o.data_ptr(),
                                        1, 12, 1024, 128, causal, h), steps, warm, dist, stream)
             flops = (2.0 * 12 * 128 * 1024 * 1025) if causal else 4.0 * 12 * 1024 * 1024 * 128
-            record(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}", ms, flops,
-                   "tensor" if tag == "f16" else "ffma", tc if tag == "f16" else ffma,
-                   "TFLOP/s", note="causal-exact FLOPs" if causal else None,
+            name = f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}"
+            record(name, ms, flops, tc if tag == "f16" else ffma, "TFLOP/s",
                    world_units=dist.world, sets=(len(qkv), set_bytes))
+            fn(*(x.data_ptr() for x in qkv[0]), o.data_ptr(), 1, 12, 1024, 128, causal, h)
+            got = sync_host(o)
+            rows = np.unique(np.r_[0, 1023, np.linspace(1, 1022, 14).astype(int)])
+            oks, errs = [], []
+            for head in (0, 5, 11):
+                ref = orc.attention_rows(*(x[0, head].astype(np.float32) for x in qkv0),
+                                         causal, rows)
+                g = got[0, head, rows]
+                if tag == "f16":
+                    ok, e = _f16_gate(g, ref.astype(np.float64))
+                else:  # the reference's FP32 attention gate (tests/attention_smoke.cu:108)
+                    e = float(np.abs(g - ref).max())
+                    ok = bool(np.all(np.abs(g - ref) <= 1e-4 + 1e-4 * np.abs(ref)))
+                oks.append(ok)
+                errs.append(e)
+            parity[name] = [all(oks), float(f"{max(errs):.2e}")]
         del qkv
 
     # sharded causal attention B8 H32 S4096 D128 (strong scaling over B*H)
@@ -636,36 +744,61 @@ def extras(args, dist, dev, peaks, only: set[str]):
         total_heads, s_len, d = 8 * 32, 4096, 128
         b0, b1 = shard_range(total_heads, dist.world, dist.rank)
         mine = b1 - b0
-        q, k_, v = (t(rng.normal(0, 1, (mine, s_len, d)).astype(np.float16)) for _ in range(3))
+        # Heads are generated per global head index so any N gives the same data.
+        qkv_h = [np.empty((mine, s_len, d), dtype=np.float16) for _ in range(3)]
+        for j, head in enumerate(range(b0, b1)):
+            hr = np.random.default_rng(9000 + head)
+            for x in qkv_h:
+                x[j] = hr.standard_normal((s_len, d), dtype=np.float32).astype(np.float16)
+        q, k_, v = (t(x) for x in qkv_h)
         o = torch.empty((mine, s_len, d), device=dev)
         ms = _measure(lambda i, h: lib.opl_attention_f16(q.data_ptr(), k_.data_ptr(), v.data_ptr(),
                                                       o.data_ptr(), 1, mine, s_len, d, 1, h),
                       max(3, steps // 4), 2, dist, stream)
         flops = 2.0 * total_heads * d * s_len * (s_len + 1)
-        rate = flops / (ms * 1e-3) / 1e12
-        out["attn_sharded_b8h32s4096d128_causal"] = {
-            "ms": round(ms, 4), "value": round(rate, 2), "unit": "TFLOP/s", "bound": "tensor",
-            "frac_per_gpu": round(rate / dist.world / tc, 4), "scaling": "strong",
-            "heads_per_rank": mine, "note": "causal-exact FLOPs; dense-count = 2x"}
-        del q, k_, v, o
+        record("attn_sharded_b8h32s4096d128_causal", ms, flops, tc, "TFLOP/s",
+               world_units=dist.world, heads_per_rank=mine)
+        # Parity on this rank's own shard: 2 heads x 10 sampled query rows
+        # (first, last and spread rows), the oracle's exact per-row loop.
+        torch.cuda.synchronize()
+        rows = np.unique(np.r_[0, s_len - 1, np.linspace(1, s_len - 2, 8).astype(int)])
+        oks, errs = [], []
+        for j in (0, mine - 1):
+            ref = orc.attention_rows(*(x[j].astype(np.float32) for x in qkv_h), True, rows)
+            g = o[j][torch.from_numpy(rows).to(dev)].cpu().numpy()
+            ok, e = _f16_gate(g, ref.astype(np.float64))
+            oks.append(ok)
+            errs.append(e)
+        parity["attn_sharded_b8h32s4096d128_causal"] = [all(oks), float(f"{max(errs):.2e}")]
+        del q, k_, v, o, qkv_h
 
     # sharded FP16 GEMM 16384^3 (strong scaling over M row blocks, B replicated)
     if want("gemm_sharded"):
         M = N = K = 16384
         m0, m1 = shard_range(M, dist.world, dist.rank)
-        a = t((rng.uniform(-1, 1, (m1 - m0, K)) / np.sqrt(K)).astype(np.float16))
-        b = t((rng.uniform(-1, 1, (K, N)) / np.sqrt(K)).astype(np.float16))
+        # A row blocks from a per-row-block seed, B from a fixed seed: same
+        # global matrices at any N.  Generated on the GPU (1.5 GiB of FP16).
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(31337)
+        b = ((torch.rand((K, N), device=dev, generator=gen) * 2 - 1) / np.sqrt(K)).half()
+        gen.manual_seed(4242 + m0)
+        a = ((torch.rand((m1 - m0, K), device=dev, generator=gen) * 2 - 1) / np.sqrt(K)).half()
         cc = torch.empty((m1 - m0, N), device=dev)
         ms = _measure(lambda i, h: lib.opl_gemm_f16(a.data_ptr(), b.data_ptr(), cc.data_ptr(),
                                                  m1 - m0, N, K, h), 3, 1, dist, stream)
-        rate = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-        out["gemm_sharded_f16_16384"] = {
-            "ms": round(ms, 4), "value": round(rate, 2), "unit": "TFLOP/s", "bound": "tensor",
-            "frac_per_gpu": round(rate / dist.world / tc, 4), "scaling": "strong",
-            "rows_per_rank": m1 - m0}
+        record("gemm_sharded_f16_16384", ms, 2.0 * M * N * K, tc, "TFLOP/s",
+               world_units=dist.world, rows_per_rank=m1 - m0)
+        # Parity on this rank's own rows: 16 sampled rows vs the FP64 product.
+        torch.cuda.synchronize()
+        idx = np.unique(np.linspace(0, m1 - m0 - 1, 16).astype(int))
+        ti = torch.from_numpy(idx).to(dev)
+        a_rows = a[ti].double().cpu().numpy()
+        ref = a_rows @ b.double().cpu().numpy()
+        ok, e = _f16_gate(cc[ti].cpu().numpy(), ref)
+        parity["gemm_sharded_f16_16384"] = [ok, float(f"{e:.2e}")]
         del a, b, cc
     torch.cuda.empty_cache()
-    return out
+    return out, parity
 
 
 # ------------------------------------------------------------ reference on B200
@@ -827,8 +960,9 @@ def cpu_ops_records(budget_s: float = 1.5) -> dict:
     rng = np.random.default_rng(77)
     out = {}
 
-    def timed(fn):
-        fn()
+    def timed(fn, warm=True):
+        if warm:
+            fn()
         times, t_start = [], time.perf_counter()
         while True:
             t0 = time.perf_counter()
@@ -838,7 +972,8 @@ def cpu_ops_records(budget_s: float = 1.5) -> dict:
                 return statistics.median(times), len(times)
 
     def rec(name, value, unit, cores, knd, sample, extrapolated=False):
-        r = {"value": round(value, 4), "unit": unit, "cores": cores, "kind": knd,
+        # sample: what was run, kept short (it is printed on the bench line)
+        r = {"value": float(f"{value:.4g}"), "unit": unit, "cores": cores, "kind": knd,
              "sample": sample}
         if extrapolated:
             r["extrapolated"] = True
@@ -855,7 +990,7 @@ def cpu_ops_records(budget_s: float = 1.5) -> dict:
     x = rng.uniform(-1, 1, n).astype(np.float32)
     red = L.ref_cpu_reduce_sum if ref is not None else L.oracle_reduce_sum
     sec, k = timed(lambda: split_rows(n, lambda a, b: red(F(x[a:]), b - a)))
-    rec("reduce_16M", n * 4 / sec / 1e9, "GB/s", threads, kind, f"{k} full runs, chunks per thread")
+    rec("reduce_16M", n * 4 / sec / 1e9, "GB/s", threads, kind, f"{k} runs")
 
     # ragged row ops 4097 x 1023
     r, c = 4097, 1023
@@ -895,21 +1030,20 @@ def cpu_ops_records(budget_s: float = 1.5) -> dict:
             for tag in ("f16", "f32"):
                 rec(f"attention_{tag}_b1h12s1024d128{'_causal' if causal else ''}",
                     flops / sec / 1e12, "TFLOP/s", heads, kind,
-                    f"{heads} of 12 heads (one per thread), {k} runs; rate scales with "
-                    f"heads up to the core count", extrapolated=heads < 12)
+                    f"{heads}/12 heads, {k} runs", extrapolated=heads < 12)
 
     # BF16 row ops through torch CPU (the reference has no 16-bit row ops)
     tt = torch.get_num_threads()
     xb = torch.from_numpy(rng.normal(0, 1, (4096, 1024)).astype(np.float32)).to(torch.bfloat16)
     sec, k = timed(lambda: torch.softmax(xb, dim=-1))
     rec("softmax_bf16_4096x1024", 2 * xb.numel() * 2 / sec / 1e9, "GB/s", tt, "torch-cpu",
-        f"torch.softmax BF16, {k} runs")
+        f"{k} runs")
     xr16 = torch.from_numpy(rng.normal(0, 1, (2048, 4096)).astype(np.float32)).to(torch.bfloat16)
     wr16 = torch.ones(4096, dtype=torch.bfloat16)
     sec, k = timed(lambda: xr16 * torch.rsqrt(xr16.float().pow(2).mean(-1, keepdim=True)
                                               + RMS_EPS).to(torch.bfloat16) * wr16)
     rec("rmsnorm_bf16_2048x4096", (2 * xr16.numel() + 4096) * 2 / sec / 1e9, "GB/s", tt,
-        "torch-cpu", f"RMSNorm formula in torch BF16 (FP32 sum of squares), {k} runs")
+        "torch-cpu", f"{k} runs")
 
     # GEMMs through torch CPU matmul (FP32 math), a row slice of A
     for name, (m, nn, kd), rows in (("gemm_f16_4096", (4096, 4096, 4096), 64),
@@ -922,11 +1056,35 @@ def cpu_ops_records(budget_s: float = 1.5) -> dict:
         sec, k = timed(lambda: torch.matmul(a_, b_))
         if "_m" in name:
             rec(name, (2 * (rows * kd + kd * nn) + 4 * rows * nn) / sec / 1e9, "GB/s", tt,
-                "torch-cpu", f"torch.matmul FP32, {k} runs")
+                "torch-cpu", f"{k} runs")
         else:
             rec(name, 2.0 * rows * nn * kd / sec / 1e12, "TFLOP/s", tt, "torch-cpu",
-                f"torch.matmul FP32 on {rows} of {m} rows, {k} runs, scaled",
-                extrapolated=True)
+                f"{rows}/{m} rows, {k} runs", extrapolated=True)
+    # Sharded configs on a 1/64 slice, scaled linearly (extrapolated):
+    # causal attention B8H32S4096D128 -> 4 of 256 heads through the
+    # reference's loop, one head per thread; GEMM 16384^3 -> 256 of 16384
+    # rows of A through torch CPU matmul (FP32).
+    if ref is not None:
+        s_, d_, heads = 4096, 128, 4
+        q, kk, v = (rng.normal(0, 1, (heads, s_, d_)).astype(np.float32) for _ in range(3))
+        o = np.empty_like(q)
+
+        def att_slice():
+            jobs = [pool.submit(ref.ref_cpu_attention, F(q[h]), F(kk[h]), F(v[h]), F(o[h]),
+                                1, 1, s_, d_, 1) for h in range(heads)]
+            for j in jobs:
+                j.result()
+        sec, k = timed(att_slice, warm=False)
+        rec("attn_sharded_b8h32s4096d128_causal", 2.0 * heads * d_ * s_ * (s_ + 1) / sec / 1e12,
+            "TFLOP/s", heads, kind, f"4/256 heads, {k} runs", extrapolated=True)
+        del q, kk, v, o
+    rows, nk = 256, 16384
+    a_ = torch.empty((rows, nk)).uniform_(-1, 1)
+    b_ = torch.empty((nk, nk)).uniform_(-1, 1)
+    sec, k = timed(lambda: torch.matmul(a_, b_))
+    rec("gemm_sharded_f16_16384", 2.0 * rows * nk * nk / sec / 1e12, "TFLOP/s", tt,
+        "torch-cpu", f"{rows}/{nk} rows, {k} runs", extrapolated=True)
+    del a_, b_
     pool.shutdown()
     return out
 
@@ -964,9 +1122,10 @@ def cpu_torch_record(budget_s: float = 5.0, max_steps: int = 100) -> dict:
 
 # ------------------------------------------------------------ main
 
-def committed_traffic(kernel: str):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary
-    (profiles/dram_traffic.json), or None."""
+def measured_traffic(kernel: str):
+    """DRAM bytes (read + write) per launch of `kernel`, from the committed
+    ncu summary profiles/dram_traffic.json (averaged over consecutive
+    launches on rotating buffers so write-backs are counted), or None."""
     try:
         data = json.loads((REPO / "profiles" / "dram_traffic.json").read_text())
         return data[kernel]["dram_bytes_per_launch"]
@@ -1002,12 +1161,40 @@ def run_reference(args, dist) -> int:
     return 0
 
 
+OPS_FMT = ("ops[name] = [ms per launch, value (GB/s if hbm-bound else TFLOP/s, all ranks), "
+           "fraction of the measured per-GPU peak, CPU value in the same unit "
+           "(null if none), CPU tag kind/cores[/x = slice, extrapolated], "
+           "max error vs the CPU oracle over all ranks' own outputs (gate: parity_ok)]")
+
+
+def compact_ops(ops: dict, cpu: dict, parity: dict | None = None) -> dict:
+    """One short list per config (OPS_FMT) so the whole line stays short."""
+    tags = {"reference": "ref", "port": "port", "torch-cpu": "torch"}
+    res = {}
+    for name, r in ops.items():
+        c = cpu.get(name)
+        entry = [r["ms"], r["value"], r["frac"]]
+        if c is None:
+            entry += [None, None]
+        else:
+            tag = f"{tags.get(c['kind'], c['kind'])}/{c['cores']}"
+            entry += [c["value"], tag + ("/x" if c.get("extrapolated") else "")]
+        p = (parity or {}).get(name)
+        entry.append(None if p is None else p[1])
+        res[name] = entry
+    return res
+
+
 def run_ours(args, dist) -> int:
     import torch
 
     import operatorlib
 
     operatorlib.capi()  # fail loudly if the CUDA library is missing
+    if dist.world > 1:
+        # Communicator set-up lines (rank count, transport) in the log.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     dist.init("nccl")
     dev = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(dev)
@@ -1015,23 +1202,29 @@ def run_ours(args, dist) -> int:
     only = {s for s in args.only.split(",") if s}
     with ClockSampler(dist.local_rank) as clocks:
         head = bench_rowops(args, dist, dev, peaks)
-        ops = {} if args.no_extras else extras(args, dist, dev, peaks, only)
+        ops, parity = ({}, {}) if args.no_extras else extras(args, dist, dev, peaks, only)
         ref = ref_b200(args, dist, dev, peaks) if (dist.world == 1 and not args.no_extras
                                                    and not only) else None
-    code = ctypes_int = None
     import ctypes
 
     ctypes_int = ctypes.c_int(0)
     code = operatorlib.capi().opl_read_and_clear_watchdog(ctypes_int)
     watchdog = ctypes_int.value if code == 0 else f"read failed ({code})"
-    cpu = (cpu_baseline_record() if (dist.rank == 0 and dist.world == 1 and not args.no_cpu)
-           else None)
-    cpu_torch = (cpu_torch_record()
-                 if (dist.rank == 0 and dist.world == 1 and not args.no_cpu) else None)
+    # Parity of every rank's own outputs: a config passes only if it passed
+    # on all ranks; the error shown is the max over ranks.
+    par_all = {}
+    for name in sorted(parity):
+        ok, err = parity[name]
+        par_all[name] = [dist.all_true(ok), float(f"{dist.max(err):.2e}")]
+    cpu_on = dist.rank == 0 and dist.world == 1 and not args.no_cpu
+    cpu = cpu_baseline_record() if cpu_on else None
+    cpu_torch = cpu_torch_record() if cpu_on else None
+    cpu_ops = cpu_ops_records() if (cpu_on and ops) else {}
     if dist.rank == 0:
         value = STEP_BYTES * dist.world / (head["ms"] * 1e-3) / 1e9
         e2e = STEP_BYTES * dist.world / (head["e2e_ms"] * 1e-3) / 1e9
         peak = peaks["hbm_gbs"]
+        traffic = measured_traffic(head["dominant"])
         line = {
             "metric": "row-op HBM GB/s (softmax+rmsnorm+transpose, BASELINE configs[1])",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": dist.world,
@@ -1040,24 +1233,17 @@ def run_ours(args, dist) -> int:
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {
                 "workload": WORKLOAD,
-                "per_rank": "each rank owns its own full row set (row-sharded, no collective)",
-                "l2": f"inputs rotate over {head['n_sets']} buffer sets "
-                      f"({head['n_sets'] * STEP_BYTES / 2**20:.0f} MiB > 2x L2)",
-                "algorithmic_bytes_per_step_per_rank": STEP_BYTES,
+                "l2": f"{head['n_sets']} rotating sets, {head['n_sets'] * STEP_BYTES >> 20} MiB",
+                "bytes_per_step_per_rank": STEP_BYTES,
             },
             "e2e": {"value": round(e2e, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"],
-                    "path": "C-ABI calls with pinned-host H2D of inputs and D2H of outputs, "
-                            "pipelined over copy-in / compute / copy-out streams"},
+                    "h2d_bytes_per_step": head["h2d"], "d2h_bytes_per_step": head["d2h"]},
             "roofline": {"bound": "hbm", "kernel": head["dominant"],
                          "achieved": round(head["dominant_gbs"], 1), "peak": peak,
                          "unit": "GB/s", "frac": round(head["dominant_gbs"] / peak, 4),
-                         "traffic": committed_traffic(head["dominant"]),
-                         "algorithmic_bytes": head["dominant_bytes"],
-                         "peak_source": f"{peaks['source']} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"
-                         if peaks["source"] == "measured" else "fallback 6.65 TB/s"},
+                         "traffic": traffic, "algorithmic_bytes": head["dominant_bytes"],
+                         "peak_source": peaks["source"]},
             "per_kernel_gbs": head["per_kernel_gbs"],
-            "per_kernel_ms": head["per_kernel_ms"],
             "gpu_launches": 3 * args.steps,
             "clocks": clocks.summary(head["t0"], head["t1"], head["t_kernels"]),
             "watchdog": watchdog,
@@ -1065,15 +1251,24 @@ def run_ours(args, dist) -> int:
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if cpu_torch is not None:
-            line["cpu_torch"] = cpu_torch
-        if ops and dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-            for name, r in cpu_ops_records().items():
-                if name in ops:
-                    ops[name]["cpu"] = r
-        if ops:
-            line["ops"] = ops
+            line["cpu_torch"] = {k: cpu_torch[k] for k in ("value", "unit", "cores", "kind")}
+        if par_all:
+            line["parity_ok"] = all(v[0] for v in par_all.values())
+            failed = [k for k, v in par_all.items() if not v[0]]
+            if failed:
+                line["parity_failed"] = failed
         if ref is not None:
-            line["ref_b200"] = ref
+            line["ref_b200"] = {k: v["value"] for k, v in ref.items()
+                                if isinstance(v, dict)} or ref
+        if ops:
+            line["ops_fmt"] = OPS_FMT
+            line["ops"] = compact_ops(ops, cpu_ops, par_all)
+        # Details that do not fit the one-line summary go to stderr.
+        print(json.dumps({"bench_detail": {"ops": ops, "cpu_ops": cpu_ops,
+                                           "parity": par_all,
+                                           "cpu_torch": cpu_torch,
+                                           "per_kernel_ms": head["per_kernel_ms"]}}),
+              file=sys.stderr, flush=True)
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.close()
@@ -1114,20 +1309,28 @@ def run_profile(args) -> int:
                           bsz, hd, sq, d, causal, h)
     elif op == "reduce":
         n = shape[0] if shape else 16_777_216
-        x = t(rng.uniform(-1, 1, n).astype(np.float32))
+        xs = [t(rng.uniform(-1, 1, n).astype(np.float32)) for _ in range(args.sets)]
         r = torch.empty((), device=dev)
-        call = lambda: lib.opl_reduce_sum_f32(x.data_ptr(), r.data_ptr(), n, h)
+        it = iter(range(1 << 62))
+        call = lambda: lib.opl_reduce_sum_f32(xs[next(it) % args.sets].data_ptr(),
+                                              r.data_ptr(), n, h)
     elif op in ("softmax", "rmsnorm", "transpose"):
         rows, cols = shape or {"softmax": SOFTMAX_SHAPE, "rmsnorm": RMS_SHAPE,
                                "transpose": TRANSPOSE_SHAPE}[op]
-        x = t(rng.normal(0, 1, (rows, cols)).astype(np.float32))
+        xs = [t(rng.normal(0, 1, (rows, cols)).astype(np.float32)) for _ in range(args.sets)]
+        ys = [torch.empty((rows, cols), device=dev) for _ in range(args.sets)]
         w = t(rng.normal(1, 0.1, cols).astype(np.float32))
-        y = torch.empty((rows, cols), device=dev)
-        call = {"softmax": lambda: lib.opl_softmax_f32(x.data_ptr(), y.data_ptr(), rows, cols, h),
-                "rmsnorm": lambda: lib.opl_rmsnorm_f32(x.data_ptr(), w.data_ptr(), y.data_ptr(),
-                                                       rows, cols, RMS_EPS, h),
-                "transpose": lambda: lib.opl_transpose_f32(x.data_ptr(), y.data_ptr(), rows,
-                                                           cols, h)}[op]
+        it = iter(range(1 << 62))
+
+        def call():
+            i = next(it) % args.sets
+            x, y = xs[i], ys[i]
+            if op == "softmax":
+                return lib.opl_softmax_f32(x.data_ptr(), y.data_ptr(), rows, cols, h)
+            if op == "rmsnorm":
+                return lib.opl_rmsnorm_f32(x.data_ptr(), w.data_ptr(), y.data_ptr(), rows,
+                                           cols, RMS_EPS, h)
+            return lib.opl_transpose_f32(x.data_ptr(), y.data_ptr(), rows, cols, h)
     elif op in ("softmax_bf16", "rmsnorm_bf16"):
         rows, cols = shape or {"softmax_bf16": SOFTMAX_SHAPE, "rmsnorm_bf16": RMS_SHAPE}[op]
         x = t(rng.normal(0, 1, (rows, cols)).astype(np.float32)).to(torch.bfloat16)

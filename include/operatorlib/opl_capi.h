@@ -53,11 +53,12 @@ int opl_reduce_sum_partial_f64(const float* input, double* output, size_t n,
  * inside allocator hooks or pool callbacks, frameworks that own all device
  * memory, fixed memory budgets).  Partial sums go to a fixed file-scope
  * device array of 4096 FP64 slots (32 KiB, held by every GPU that loads the
- * library until exit); a call needing more slots (a device with more than
- * 4096 SMs) returns cudaErrorInvalidValue.  The first call on each device
- * looks the array up (cudaGetSymbolAddress) and must come before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race;
- * serialise them on one stream.  Same result as opl_reduce_sum_f32. */
+ * library until exit); the partial-sum grid never exceeds 4096 CTAs, so any
+ * n fits.  The first call on each device looks the array up
+ * (cudaGetSymbolAddress), caches the address and must come before any stream
+ * capture; the cached address does not survive cudaDeviceReset.  All calls
+ * share the array: calls that overlap on the GPU race; serialise them on one
+ * stream.  Bit-identical result to opl_reduce_sum_f32. */
 int opl_reduce_sum_f32_noalloc(const float* input, float* output, size_t n,
                                opl_stream_t stream);
 
@@ -70,7 +71,10 @@ int opl_reduce_sum_f32_noalloc(const float* input, float* output, size_t n,
  * opl_team_reduce_sum_f32 on its own chunk, in the same order on all ranks:
  * each GPU sums its chunk, exchanges the FP64 partial with the peers over
  * NVLink and writes the identical total to *output.  A peer that does not
- * arrive within a bounded wait yields NaN and the watchdog code. */
+ * arrive within a bounded wait (about 2 s) yields NaN and the watchdog code.
+ * A timeout is final for the team: every later call on that rank returns NaN
+ * at once, the other ranks time out on their next call and do the same, and
+ * the team has to be destroyed (opl_team_destroy) and created again. */
 int opl_team_create(int rank, int world, void** team, void* ipc_handle_out);
 int opl_team_connect(void* team, const void* all_ipc_handles);
 int opl_team_reduce_sum_f32(void* team, const float* input, float* output, size_t n,

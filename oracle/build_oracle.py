@@ -9,9 +9,10 @@ Outputs (all git-ignored build products; they travel with the tree):
   oracle/_ref/libref_cpu.so        the reference's own CPU verification loops,
                                    compiled from its standalone sources in
                                    place (ref_shim/ref_cpu_*.cu).
-The two _ref libraries are built only where the reference tree exists
-(OPL_REFERENCE_ROOT, default the read-only mount used while developing);
-elsewhere the prebuilt copies are used as they are.  No reference source is
+The two _ref libraries are built only where the reference tree exists: the
+directory named by --reference-root or OPL_REFERENCE_ROOT, else a checkout
+named `reference` beside this repository's directory.  Elsewhere the
+prebuilt copies are used as they are, silently.  No reference source is
 copied: each file is compiled where it lies.
 """
 from __future__ import annotations
@@ -37,8 +38,9 @@ REF_SRC = ["reduce.cu", "softmax.cu", "transpose.cu", "rmsnorm.cu", "gemm.cu",
            "attention.cu"]
 
 
-def reference_root() -> Path | None:
-    root = Path(os.environ.get("OPL_REFERENCE_ROOT", "/root/reference"))
+def reference_root(explicit: str | None = None) -> Path | None:
+    given = explicit or os.environ.get("OPL_REFERENCE_ROOT")
+    root = Path(given) if given else ORACLE.parent.parent / "reference"
     return root if (root / "src" / "reduce.cu").exists() else None
 
 
@@ -62,8 +64,8 @@ def build_oracle() -> Path:
     return lib
 
 
-def build_reference() -> list[Path]:
-    root = reference_root()
+def build_reference(reference: str | None = None) -> list[Path]:
+    root = reference_root(reference)
     if root is None:
         return []
     REF_OUT.mkdir(exist_ok=True)
@@ -98,9 +100,15 @@ def build_reference() -> list[Path]:
     return built
 
 
-def main() -> int:
+def main(argv=None) -> int:
+    import argparse
+
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--reference-root", default=None,
+                   help="reference checkout to compile oracle/_ref from")
+    args = p.parse_args(argv)
     print(build_oracle())
-    for p in build_reference():
+    for p in build_reference(args.reference_root):
         print(p)
     return 0
 

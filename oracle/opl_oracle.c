@@ -64,35 +64,52 @@ void oracle_rmsnorm(const float* in, const float* w, float* out, int tokens,
  * dot(q, k) * (1 / sqrt(d)), causal rows see keys 0..row, double max, exp,
  * denominator, then out = (float)(sum_j p_j v_j / denominator).
  * heads = batch * heads; tensors are contiguous [heads, s, d]. */
+static void attention_row(const float* q, const float* k, const float* v,
+                          float* out_row, int s, int d, int causal, int row,
+                          double* scores) {
+  const double scale = 1.0 / sqrt((double)d);
+  const int visible = causal ? row + 1 : s;
+  double m = -INFINITY;
+  for (int col = 0; col < visible; ++col) {
+    double dot = 0.0;
+    for (int x = 0; x < d; ++x)
+      dot += (double)q[(size_t)row * d + x] * k[(size_t)col * d + x];
+    scores[col] = dot * scale;
+    if (scores[col] > m) m = scores[col];
+  }
+  double den = 0.0;
+  for (int col = 0; col < visible; ++col) {
+    scores[col] = exp(scores[col] - m);
+    den += scores[col];
+  }
+  for (int x = 0; x < d; ++x) {
+    double acc = 0.0;
+    for (int col = 0; col < visible; ++col)
+      acc += scores[col] * v[(size_t)col * d + x];
+    out_row[x] = (float)(acc / den);
+  }
+  (void)s;
+}
+
 void oracle_attention(const float* q, const float* k, const float* v,
                       float* out, int heads, int s, int d, int causal,
                       double* scores /* scratch of s doubles */) {
-  const double scale = 1.0 / sqrt((double)d);
   for (int h = 0; h < heads; ++h) {
     const size_t base = (size_t)h * s * d;
-    for (int row = 0; row < s; ++row) {
-      const int visible = causal ? row + 1 : s;
-      double m = -INFINITY;
-      for (int col = 0; col < visible; ++col) {
-        double dot = 0.0;
-        for (int x = 0; x < d; ++x)
-          dot += (double)q[base + (size_t)row * d + x] * k[base + (size_t)col * d + x];
-        scores[col] = dot * scale;
-        if (scores[col] > m) m = scores[col];
-      }
-      double den = 0.0;
-      for (int col = 0; col < visible; ++col) {
-        scores[col] = exp(scores[col] - m);
-        den += scores[col];
-      }
-      for (int x = 0; x < d; ++x) {
-        double acc = 0.0;
-        for (int col = 0; col < visible; ++col)
-          acc += scores[col] * v[base + (size_t)col * d + x];
-        out[base + (size_t)row * d + x] = (float)(acc / den);
-      }
-    }
+    for (int row = 0; row < s; ++row)
+      attention_row(q + base, k + base, v + base, out + base + (size_t)row * d, s,
+                    d, causal, row, scores);
   }
+}
+
+/* The same per-row computation for selected query rows of ONE head
+ * ([s, d] q/k/v): out[i] is the output row of query rows[i].  Lets callers
+ * check sampled rows of heads too long for a full CPU pass. */
+void oracle_attention_rows(const float* q, const float* k, const float* v,
+                           float* out, int s, int d, int causal,
+                           const int* rows, int nrows, double* scores) {
+  for (int i = 0; i < nrows; ++i)
+    attention_row(q, k, v, out + (size_t)i * d, s, d, causal, rows[i], scores);
 }
 
 /* GEMM: the reference's oracle is cuBLAS (gemm/gemm_common.h:80-86,153-160;

@@ -52,6 +52,10 @@ def lib() -> ctypes.CDLL:
             L.oracle_attention.argtypes = [_F, _F, _F, _F, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, _D]
+            L.oracle_attention_rows.argtypes = [_F, _F, _F, _F, ctypes.c_int,
+                                                ctypes.c_int, ctypes.c_int,
+                                                ctypes.POINTER(ctypes.c_int),
+                                                ctypes.c_int, _D]
             L.oracle_gemm_rows.argtypes = [_F, _F, _D] + [ctypes.c_int] * 5
             L.oracle_half_to_float.restype = ctypes.c_float
             L.oracle_half_to_float.argtypes = [ctypes.c_uint16]
@@ -146,6 +150,20 @@ def attention(q, k, v, causal: bool) -> np.ndarray:
     scratch = np.empty(s, dtype=np.float64)
     lib().oracle_attention(_fp(q), _fp(k), _fp(v), _fp(out), b * h, s, d,
                            int(causal), _dp(scratch))
+    return out
+
+
+def attention_rows(q, k, v, causal: bool, rows) -> np.ndarray:
+    """Output rows `rows` of one head: q, k, v float32 [S, D]; returns
+    [len(rows), D], each row computed exactly as attention() computes it."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    s, d = q.shape
+    idx = np.ascontiguousarray(rows, dtype=np.int32)
+    out = np.empty((idx.size, d), dtype=np.float32)
+    scratch = np.empty(s, dtype=np.float64)
+    lib().oracle_attention_rows(_fp(q), _fp(k), _fp(v), _fp(out), s, d, int(causal),
+                                idx.ctypes.data_as(ctypes.POINTER(ctypes.c_int)),
+                                idx.size, _dp(scratch))
     return out
 
 

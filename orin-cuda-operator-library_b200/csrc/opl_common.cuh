@@ -62,6 +62,13 @@ __device__ __forceinline__ void watchdog_trip(int* word, int code) {
   atomicCAS(word, 0, code);
 }
 
+// Global nanosecond timer (%globaltimer), for wall-time bounds on spin-waits.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 // Device address of the current device's watchdog word (nullptr on error).
 int* watchdog_word();
 

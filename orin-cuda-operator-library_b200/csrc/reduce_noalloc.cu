@@ -13,7 +13,9 @@
 // The array's name is a host-side stand-in in host code, not a device
 // address: the device address is fetched with cudaGetSymbolAddress, once per
 // device with that device current, on the first call made on that device
-// (make that first call before any stream capture), and cached.
+// (make that first call before any stream capture), and cached.  The cached
+// address does not survive cudaDeviceReset: after a reset of a device, a
+// process must not call this entry point on that device again.
 //
 // Every call shares the array and it keeps the previous call's contents.
 // Nothing needs clearing: each call writes every slot it later reads.  Calls
@@ -28,6 +30,9 @@ namespace opl {
 namespace {
 
 constexpr int kScratchSlots = 4096;
+// reduce_grid never returns more than kReduceMaxCtas CTAs, one slot each.
+static_assert(kScratchSlots >= kReduceMaxCtas,
+              "the scratch array must hold one partial per reduce CTA");
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) double g_reduce_scratch[kScratchSlots];
@@ -58,7 +63,6 @@ extern "C" int opl_reduce_sum_f32_noalloc(const float* input, float* output,
                                           size_t n, opl_stream_t stream) {
   if (input == nullptr || output == nullptr || n == 0) return cudaErrorInvalidValue;
   const int blocks = opl::reduce_grid(n);
-  if (blocks > opl::kScratchSlots) return cudaErrorInvalidValue;  // > 4096 SMs
   double* scratch = nullptr;
   const cudaError_t error = opl::scratch_address(&scratch);
   if (error != cudaSuccess) return error;

@@ -14,9 +14,18 @@
 //                                    launch is replayable in a CUDA graph)
 //   uint64 flags[kMaxTeam]           flags[r] = last call number rank r posted
 //   double slots[2][kMaxTeam]        slots[call parity][r] = rank r's partial
+//   uint64 failed                    set (locally, never by a peer) when this
+//                                    rank's wait for a peer timed out
 // A rank can post call c+1 only after it saw every flag of call c, which each
 // peer raises only after it finished reading its slots for call c-1 (same
 // parity as c+1): double-buffered slots never overwrite unread values.
+//
+// A rank whose wait timed out has not seen every flag of that call, so it may
+// never post again: its `failed` word stays set and every later call on it
+// returns NaN at once without touching the peers.  A peer still waiting for
+// it times out in turn (its own wait is bounded too) and fails the same way,
+// so after a timeout the whole team answers NaN until it is destroyed and
+// created again.
 //
 // Plain peer loads/stores only (no multimem, no TMA, no cluster multicast).
 #include <cstring>
@@ -29,13 +38,15 @@ namespace opl {
 namespace {
 
 constexpr int kMaxTeam = 8;
-constexpr uint32_t kTeamMaxPolls = 1u << 24;
+constexpr uint32_t kTeamMaxPolls = 1u << 24;              // backstop
+constexpr uint64_t kTeamMaxWaitNs = 2000ull * 1000ull * 1000ull;  // 2 s
 constexpr int kWatchdogTeam = 0x6e04;
 
 struct TeamBuffer {
   unsigned long long seq;
   unsigned long long flags[kMaxTeam];
   double slots[2][kMaxTeam];
+  unsigned long long failed;
 };
 
 struct TeamPeers {
@@ -70,6 +81,10 @@ __global__ void __launch_bounds__(kReduceThreads)
   v = local_total;
 
   TeamBuffer* mine = peers.peer[rank];
+  if (mine->failed != 0) {  // an earlier call timed out: never post again
+    if (lane == 0) *output = __int_as_float(0x7fffffff);
+    return;
+  }
   const unsigned long long call = mine->seq + 1;  // same on every rank
   const int parity = static_cast<int>(call & 1);
   if (lane < world) {
@@ -79,9 +94,11 @@ __global__ void __launch_bounds__(kReduceThreads)
   }
   bool ok = true;
   if (lane < world) {
+    const uint64_t start = globaltimer_ns();
     uint32_t polls = 0;
     while (ld_acquire_sys(&mine->flags[lane]) < call) {
-      if (++polls == kTeamMaxPolls) {
+      if (++polls == kTeamMaxPolls ||
+          ((polls & 63u) == 0u && globaltimer_ns() - start > kTeamMaxWaitNs)) {
         ok = false;
         break;
       }
@@ -92,6 +109,7 @@ __global__ void __launch_bounds__(kReduceThreads)
   if (lane == 0) {
     if (!ok) {
       watchdog_trip(watchdog, kWatchdogTeam);
+      mine->failed = 1;
       *output = __int_as_float(0x7fffffff);  // NaN marks the failed exchange
     } else {
       double total = 0.0;

@@ -14,9 +14,12 @@ namespace tc {
 // Watchdog codes written when a bounded wait gives up.
 constexpr int kWatchdogGemm = 0x6e01;
 constexpr int kWatchdogAttention = 0x6e02;
-// Polls of mbarrier.try_wait (each may suspend the thread for a while) before
-// a wait is declared hung.  Far beyond any legitimate wait in these kernels.
+// A wait is declared hung after kMaxWaitNs of wall time (read from
+// %globaltimer every 256 polls), or after kMaxPolls polls of
+// mbarrier.try_wait as a backstop.  Both are far beyond any legitimate wait
+// in these kernels (the longest is one output tile, microseconds).
 constexpr uint32_t kMaxPolls = 1u << 26;
+constexpr uint64_t kMaxWaitNs = 1500ull * 1000ull * 1000ull;  // 1.5 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -53,16 +56,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Gives up after
-// kMaxPolls polls, or at once when *abort is set by another thread of the
+// kMaxWaitNs (or kMaxPolls polls), or at once when *abort is set by another thread of the
 // CTA; on giving up it sets *abort and records `code` in the watchdog word.
 // Returns false when the wait was abandoned.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort, int* watchdog,
                                           int code) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t polls = 0; polls < kMaxPolls; ++polls) {
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t polls = 1; polls < kMaxPolls; ++polls) {
     if (mbar_try_wait(addr, parity)) return true;
-    if ((polls & 255u) == 255u && *abort) return false;
+    if ((polls & 255u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - start > kMaxWaitNs) break;
+    }
   }
   *abort = 1;
   if (watchdog != nullptr) watchdog_trip(watchdog, code);
@@ -320,9 +328,14 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort, int* watchdog, int code) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t polls = 0; polls < kMaxPolls; ++polls) {
+  if (mbar_try_wait_cluster(addr, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t polls = 1; polls < kMaxPolls; ++polls) {
     if (mbar_try_wait_cluster(addr, parity)) return true;
-    if ((polls & 255u) == 255u && *abort) return false;
+    if ((polls & 255u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - start > kMaxWaitNs) break;
+    }
   }
   *abort = 1;
   if (watchdog != nullptr) watchdog_trip(watchdog, code);

@@ -8,6 +8,8 @@
 // row writes and the column gathers at most 2-way bank-conflicted.  Other
 // shapes use a 32x32 tile with 32-bit accesses (still 128-byte coalesced per
 // warp) and bounds checks.
+#include <algorithm>
+
 #include "opl_common.cuh"
 
 namespace opl {
@@ -20,11 +22,14 @@ __global__ void __launch_bounds__(kT4Threads)
                           float* __restrict__ output, int rows, int cols) {
   __shared__ float tile[kT4][kT4 + 1];
   const int tile_col = blockIdx.x * kT4;  // input column origin
-  const int tile_row = blockIdx.y * kT4;  // input row origin
   const int c4 = threadIdx.x & 15;        // float4 column inside the tile
   const int r0 = threadIdx.x >> 4;        // 0..15
   const int cols4 = cols >> 2;
   const int rows4 = rows >> 2;
+  // grid.y is capped at 65535: taller inputs loop over their row tiles.
+  for (long long tr = static_cast<long long>(blockIdx.y) * kT4; tr < rows;
+       tr += static_cast<long long>(gridDim.y) * kT4) {
+  const int tile_row = static_cast<int>(tr);  // input row origin
 
   // Load: 64 rows x 16 float4, four passes of 16 rows.
   float4 x[4];
@@ -64,6 +69,8 @@ __global__ void __launch_bounds__(kT4Threads)
                 y);
     }
   }
+  __syncthreads();  // the tile is refilled by the next row tile
+  }
 }
 
 constexpr int kT1 = 32;
@@ -74,7 +81,11 @@ __global__ void __launch_bounds__(kT1 * kT1Rows)
                             float* __restrict__ output, int rows, int cols) {
   __shared__ float tile[kT1][kT1 + 1];
   const int x = blockIdx.x * kT1 + threadIdx.x;
-  const int y = blockIdx.y * kT1 + threadIdx.y;
+  // grid.y is capped at 65535: taller inputs loop over their row tiles.
+  for (long long r0l = static_cast<long long>(blockIdx.y) * kT1; r0l < rows;
+       r0l += static_cast<long long>(gridDim.y) * kT1) {
+  const int row0 = static_cast<int>(r0l);
+  const int y = row0 + threadIdx.y;
 #pragma unroll
   for (int k = 0; k < kT1; k += kT1Rows) {
     if (x < cols && y + k < rows)
@@ -82,13 +93,15 @@ __global__ void __launch_bounds__(kT1 * kT1Rows)
           ld_stream(input + static_cast<std::size_t>(y + k) * cols + x);
   }
   __syncthreads();
-  const int ox = blockIdx.y * kT1 + threadIdx.x;  // output column (input row)
+  const int ox = row0 + threadIdx.x;              // output column (input row)
   const int oy = blockIdx.x * kT1 + threadIdx.y;  // output row (input column)
 #pragma unroll
   for (int k = 0; k < kT1; k += kT1Rows) {
     if (ox < rows && oy + k < cols)
       st_stream(output + static_cast<std::size_t>(oy + k) * rows + ox,
                 tile[threadIdx.x][threadIdx.y + k]);
+  }
+  __syncthreads();  // the tile is refilled by the next row tile
   }
 }
 
@@ -100,13 +113,13 @@ extern "C" int opl_transpose_f32(const float* input, float* output, int rows,
   if (input == nullptr || output == nullptr || rows <= 0 || cols <= 0)
     return cudaErrorInvalidValue;
   if (rows % 4 == 0 && cols % 4 == 0 && aligned16(input) && aligned16(output)) {
-    const dim3 grid((cols + kT4 - 1) / kT4, (rows + kT4 - 1) / kT4);
-    if (grid.y > 65535) return cudaErrorInvalidValue;
+    const dim3 grid((cols + kT4 - 1) / kT4,
+                    std::min((rows + kT4 - 1) / kT4, 65535));
     transpose_vec4_kernel<<<grid, kT4Threads, 0, stream>>>(input, output, rows,
                                                             cols);
   } else {
-    const dim3 grid((cols + kT1 - 1) / kT1, (rows + kT1 - 1) / kT1);
-    if (grid.y > 65535) return cudaErrorInvalidValue;
+    const dim3 grid((cols + kT1 - 1) / kT1,
+                    std::min((rows + kT1 - 1) / kT1, 65535));
     transpose_scalar_kernel<<<grid, dim3(kT1, kT1Rows), 0, stream>>>(
         input, output, rows, cols);
   }

@@ -6,6 +6,8 @@ reduce -- while keeping its buffer alive; rank 0 launches opl_team_reduce_sum_f3
 alone.  Rank 0's finalize kernel posts its partial, waits (bounded) for a
 flag that nothing sets, gives up, writes NaN as the total and records the
 watchdog code 0x6e04; the host reads both and the context stays usable.
+The timeout is final for the team: the next call on rank 0 posts nothing
+and returns NaN at once, without waiting and without a new watchdog code.
 Only one rank ever runs a kernel, so no two kernels wait on each other.
 """
 from __future__ import annotations
@@ -15,6 +17,7 @@ import math
 import multiprocessing as mp
 import os
 import sys
+import time
 
 import pytest
 
@@ -83,6 +86,18 @@ def test_peer_that_never_posts_times_out(cuda):
         assert math.isnan(out.item())
         assert lib.opl_read_and_clear_watchdog(ctypes.byref(code)) == 0
         assert code.value == WATCHDOG_TEAM
+        # the failed team stays failed: the next call answers NaN at once
+        out.zero_()
+        t0 = time.monotonic()
+        rc = lib.opl_team_reduce_sum_f32(team, ctypes.c_void_p(x.data_ptr()),
+                                         ctypes.c_void_p(out.data_ptr()), x.numel(),
+                                         ctypes.c_void_p(stream.cuda_stream))
+        assert rc == 0
+        stream.synchronize()
+        assert time.monotonic() - t0 < 1.0  # no second bounded wait
+        assert math.isnan(out.item())
+        assert lib.opl_read_and_clear_watchdog(ctypes.byref(code)) == 0
+        assert code.value == 0
         # the context is still usable
         y = torch.empty((), device=cuda)
         operatorlib.reduce_sum_into(x, y)
