@@ -9,6 +9,12 @@ Outputs (all git-ignored build products; they travel with the tree):
   oracle/_ref/libref_cpu.so        the reference's own CPU verification loops,
                                    compiled from its standalone sources in
                                    place (ref_shim/ref_cpu_*.cu).
+  oracle/_ref/smoke/               the reference's own launcher smoke tests
+                                   (its tests/*_smoke.cu, unmodified) linked
+                                   against THIS library's static archive, and
+                                   a staged copy of its python/test_extension.py
+                                   (run unchanged against this library's
+                                   torch binding); checkers, never shipped.
 The two _ref libraries are built only where the reference tree exists: the
 directory named by --reference-root or OPL_REFERENCE_ROOT, else a checkout
 named `reference` beside this repository's directory.  Elsewhere the
@@ -100,6 +106,33 @@ def build_reference(reference: str | None = None) -> list[Path]:
     return built
 
 
+REF_SMOKE = {"core_ops_smoke": [], "attention_smoke": [], "gemm_smoke": ["-lcublas"]}
+
+
+def build_reference_smoke(reference: str | None = None) -> list[Path]:
+    """The reference's C++ smoke tests built against this library (the
+    package's liboperatorlib.a must exist: build it first)."""
+    root = reference_root(reference)
+    if root is None:
+        return []
+    import importlib.util
+    import shutil
+
+    spec = importlib.util.spec_from_file_location(
+        "opl_build", ORACLE.parent / "orin-cuda-operator-library_b200" / "build.py")
+    opl_build = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(opl_build)
+    out_dir = REF_OUT / "smoke"
+    built = [opl_build.link_against_archive(root / "tests" / f"{name}.cu", out_dir / name, extra)
+             for name, extra in REF_SMOKE.items()]
+    staged = out_dir / "test_extension.py"
+    src = root / "python" / "test_extension.py"
+    if not _newer(staged, [src]):
+        shutil.copyfile(src, staged)
+    built.append(staged)
+    return built
+
+
 def main(argv=None) -> int:
     import argparse
 
@@ -109,6 +142,8 @@ def main(argv=None) -> int:
     args = p.parse_args(argv)
     print(build_oracle())
     for p in build_reference(args.reference_root):
+        print(p)
+    for p in build_reference_smoke(args.reference_root):
         print(p)
     return 0
 

@@ -4,7 +4,13 @@ Produces, next to the Python package ``operatorlib``:
   * ``libopl_b200.so``       -- every CUDA kernel, the C-ABI (opl_*) and the
                                 C++ API of include/operatorlib/operators.h;
   * ``_operatorlib_torch.so`` -- the TORCH_LIBRARY(operatorlib, ...) binding,
-                                linked against libopl_b200.so.
+                                linked against libopl_b200.so;
+  * ``liboperatorlib.a``      -- the same objects as a static archive, the
+                                counterpart of the reference's static library
+                                target (CMakeLists.txt at the repository root
+                                builds the same archive through CMake);
+  * ``_build/bin/operatorlib_b200_smoke`` -- tests/cpp/operators_smoke.cu
+                                linked against that archive.
 
 This replaces the reference's CMake static library (CMakeLists.txt:16-36,
 CUDA_ARCHITECTURES 87) and JIT loader (python/load_extension.py:17-36): nvcc
@@ -39,6 +45,8 @@ NVCC_FLAGS = ARCH + [
     "-DOPL_BUILDING_LIBRARY",
 ]
 LIB_NAME = "libopl_b200.so"
+STATIC_NAME = "liboperatorlib.a"
+BIN_DIR = OBJ_DIR / "bin"
 TORCH_LIB_NAME = "_operatorlib_torch.so"
 
 
@@ -83,7 +91,25 @@ def build_library(force: bool = False, jobs: int = 8) -> Path:
         _run([NVCC, *ARCH, "-shared", "-cudart", "static", "-o", str(lib),
               *map(str, objects), "-Xlinker", "--no-undefined", "-lpthread",
               "-ldl", "-lrt"])
+    archive = OUT_DIR / STATIC_NAME
+    if force or _stale(archive, objects):
+        if archive.exists():
+            archive.unlink()
+        _run(["ar", "rcs", str(archive), *map(str, objects)])
     return lib
+
+
+def link_against_archive(src: Path, out: Path, extra: list[str] | None = None,
+                         force: bool = False) -> Path:
+    """Compiles a C++/CUDA test program that includes operatorlib/operators.h
+    and links it against the static archive (the way a CMake consumer of the
+    `operatorlib` target links)."""
+    archive = OUT_DIR / STATIC_NAME
+    if force or _stale(out, [src, archive]):
+        out.parent.mkdir(parents=True, exist_ok=True)
+        _run([NVCC, *ARCH, "-O2", "-std=c++17", f"-I{INCLUDE}", str(src), "-o", str(out),
+              str(archive), *(extra or [])])
+    return out
 
 
 def build_torch_binding(force: bool = False) -> Path:
@@ -115,6 +141,8 @@ def build(force: bool = False, jobs: int = 8, torch_binding: bool = True) -> Non
     if shutil.which(NVCC) is None and not Path(NVCC).exists():
         raise RuntimeError(f"nvcc not found at {NVCC}")
     build_library(force=force, jobs=jobs)
+    link_against_archive(REPO / "tests" / "cpp" / "operators_smoke.cu",
+                         BIN_DIR / "operatorlib_b200_smoke", force=force)
     if torch_binding:
         build_torch_binding(force=force)
 
