@@ -174,12 +174,69 @@ def test_attention_f32(cuda, stream, b, h, s, d, causal, qk):
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
 
 
-def test_attention_f32_baseline_shape_sampled_heads(cuda, stream):
+def test_attention_f32_baseline_shape_all_heads(cuda, stream):
+    """BASELINE FP32 attention B1 H12 S1024 D128: every head, both masks,
+    against the oracle's full loop (reference gate atol = rtol = 1e-4)."""
     q, k, v = att_inputs((1, 12, 1024, 128), None, 77, np.float32)
     for causal in (False, True):
         got = run_attention(cuda, stream, q, k, v, causal)
-        want = orc.attention(q[:, :2], k[:, :2], v[:, :2], causal)
-        np.testing.assert_allclose(got[:, :2], want, rtol=1e-4, atol=1e-4)
+        want = orc.attention(q, k, v, causal)
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+def test_gemm_f32_baseline_4096(cuda, stream):
+    """BASELINE FP32 GEMM at exactly 4096^3 (FFMA), 64 rows spread over M
+    against the FP64 product, reference gate 1e-3 + 1e-3 |ref|."""
+    rng = np.random.default_rng(4096)
+    a = (rng.uniform(-1, 1, (4096, 4096)) / 64).astype(np.float32)
+    b = (rng.uniform(-1, 1, (4096, 4096)) / 64).astype(np.float32)
+    got = run_gemm(cuda, stream, a, b)
+    idx = np.unique(np.linspace(0, 4095, 64).astype(int))
+    want = a[idx].astype(np.float64) @ b.astype(np.float64)
+    np.testing.assert_allclose(got[idx], want, rtol=1e-3, atol=1e-3)
+
+
+def test_attention_f16_sharded_config_sampled(cuda, stream):
+    """Sharded config B8 H32 S4096 D128 causal FP16 at full size: 8 heads
+    spread over B*H, 48 query rows each (first, last and spread rows, so
+    every causal key range length is represented), against the oracle's
+    per-row loop on the half-quantised inputs."""
+    import torch
+
+    b, h, s, d = 8, 32, 4096, 128
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(8324)
+    q, k, v = (torch.randn((b, h, s, d), device=cuda, generator=gen).half() for _ in range(3))
+    o = torch.empty((b, h, s, d), device=cuda)
+    operatorlib.attention_into(q, k, v, o, True)
+    stream.synchronize()
+    rows = np.unique(np.r_[0, 1, 127, 128, s - 1, np.linspace(2, s - 2, 43).astype(int)])
+    for flat in np.unique(np.linspace(0, b * h - 1, 8).astype(int)):
+        bi, hi = divmod(int(flat), h)
+        qh, kh, vh = (x[bi, hi].float().cpu().numpy() for x in (q, k, v))
+        want = orc.attention_rows(qh, kh, vh, True, rows)
+        got = o[bi, hi][torch.from_numpy(rows).to(cuda)].cpu().numpy()
+        check_f16(got, want.astype(np.float64))
+
+
+def test_gemm_f16_sharded_config_sampled(cuda, stream):
+    """Sharded config GEMM FP16 16384^3 at full size (1 GiB of C): 32 rows
+    spread over M against the FP64 product."""
+    import torch
+
+    m = n = k = 16384
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(16384)
+    a = ((torch.rand((m, k), device=cuda, generator=gen) * 2 - 1) / 128).half()
+    bm = ((torch.rand((k, n), device=cuda, generator=gen) * 2 - 1) / 128).half()
+    c = torch.empty((m, n), device=cuda)
+    operatorlib.gemm_into(a, bm, c)
+    stream.synchronize()
+    idx = torch.from_numpy(np.unique(np.linspace(0, m - 1, 32).astype(int))).to(cuda)
+    want = a[idx].cpu().numpy().astype(np.float64) @ bm.cpu().numpy().astype(np.float64)
+    check_f16(c[idx].cpu().numpy(), want)
+    del a, bm, c
+    torch.cuda.empty_cache()
 
 
 @pytest.mark.parametrize("b,h,s,d,causal", [

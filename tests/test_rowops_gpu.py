@@ -196,7 +196,9 @@ def test_rmsnorm_golden(cuda, stream, path):
 
 T_CASES = [(37, 65), (64, 96), (65, 37), (4096, 4096), (4097, 1023), (1, 1),
            (1, 1000), (1000, 1), (4, 4), (8, 12), (64, 64), (68, 132),
-           (3, 100_000), (100_000, 3), (1024, 4100)]
+           (3, 100_000), (100_000, 3), (1024, 4100),
+           # taller than 65535 row tiles: the grid loops over row tiles
+           (5_000_000, 4), (5_000_001, 3)]
 
 
 @pytest.mark.parametrize("rows,cols", T_CASES)
