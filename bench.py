@@ -565,7 +565,13 @@ def extras(args, dist, dev, peaks, only: set[str]):
             team = operatorlib.ReduceTeam(dist.rank, dist.world)
             ms = _measure(lambda i, hh: team.launch(xs[i % len(xs)], res, hh), steps, warm,
                           dist, stream)
-            record("reduce_16M", ms, 4 * n, hbm, "GB/s", world_units=dist.world)
+            # The exchange's share: the same launches without it (this rank's
+            # FP64 partial only), so time(fused) - time(local) is the cost of
+            # combining the partials over NVLink.
+            ms_local = _measure(lambda i, hh: lib.opl_reduce_sum_partial_f64(
+                xs[i % len(xs)].data_ptr(), part.data_ptr(), n, hh), steps, warm, dist, stream)
+            record("reduce_16M", ms, 4 * n, hbm, "GB/s", world_units=dist.world,
+                   exchange_us=round((ms - ms_local) * 1e3, 2))
             # every rank must hold the same total: the FP64 sum of all chunks
             team.launch(xs[0], res, h)
             got = float(sync_host(res))
@@ -1260,6 +1266,8 @@ def run_ours(args, dist) -> int:
         if ref is not None:
             line["ref_b200"] = {k: v["value"] for k, v in ref.items()
                                 if isinstance(v, dict)} or ref
+        if "reduce_16M" in ops and "exchange_us" in ops["reduce_16M"]:
+            line["reduce_exchange_us"] = ops["reduce_16M"]["exchange_us"]
         if ops:
             line["ops_fmt"] = OPS_FMT
             line["ops"] = compact_ops(ops, cpu_ops, par_all)

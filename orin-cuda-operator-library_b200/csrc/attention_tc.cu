@@ -79,18 +79,19 @@ struct AttnBars {
   int abort;
 };
 
-// K-major SW128 operand made of 64-column boxes of 128 rows: the 16-wide K
-// step kk lives in box kk/4 at byte offset 32*(kk%4).
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int kk, int box_bytes) {
-  return tc::smem_desc_sw128(base + (kk >> 2) * box_bytes + (kk & 3) * 32, 16, 1024);
-}
-
 // 2^x by the MUFU ex2 instruction (flushes subnormal results to zero;
 // 2^-inf = 0).
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
 }
 
 // Named barrier 1 over `count` threads.
@@ -115,6 +116,38 @@ __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
+}
+
+// 2^x for two values on the FMA pipe instead of MUFU, so that part of each
+// block's exponentials run beside the MUFU ones (both units busy).  Range
+// reduction: adding 1.5 * 2^23 rounds x to the nearest integer n, which then
+// sits in the low mantissa bits of the sum; f = x - n lies in [-0.5, 0.5];
+// 2^f is a degree-4 polynomial fitted for minimum relative error on that
+// interval (Lawson-weighted least squares, fitted for this kernel; 2.7e-6
+// relative, against 2^-11 for the FP16 rounding P gets next); 2^n is added
+// to the exponent field (bits(sum) << 23 keeps exactly n << 23).  Inputs
+// must lie in [-120, 120]: callers clamp at -120, where 2^x is far below
+// FP16's smallest subnormal.
+constexpr float kExpRound = 12582912.0f;  // 1.5 * 2^23
+constexpr float kExpC0 = 0.9999992847442627f;
+constexpr float kExpC1 = 0.6931218504905701f;
+constexpr float kExpC2 = 0.240247443318367f;
+constexpr float kExpC3 = 0.055917806923389435f;
+constexpr float kExpC4 = 0.009570068679749966f;
+
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x, float& y0, float& y1) {
+  const uint64_t t = add_f32x2(x, f32x2(kExpRound, kExpRound));
+  const uint64_t n = add_f32x2(t, f32x2(-kExpRound, -kExpRound));
+  const uint64_t f = fma_f32x2(n, f32x2(-1.0f, -1.0f), x);
+  uint64_t p = fma_f32x2(f32x2(kExpC4, kExpC4), f, f32x2(kExpC3, kExpC3));
+  p = fma_f32x2(p, f, f32x2(kExpC2, kExpC2));
+  p = fma_f32x2(p, f, f32x2(kExpC1, kExpC1));
+  p = fma_f32x2(p, f, f32x2(kExpC0, kExpC0));
+  float p0, p1, t0, t1;
+  split_f32x2(p, p0, p1);
+  split_f32x2(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __device__ __forceinline__ float pack_half2_bits(float lo, float hi) {
@@ -239,15 +272,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---------------------------------------------------------- MMA issuer
     bool issued_any = false;
+    // Shared-memory descriptors are built once: a K step only moves the
+    // start-address field (address / 16, bits 0-13), and smem addresses stay
+    // below 256 KB, so adding the step's offset / 16 never carries out of the
+    // field.  This keeps each MMA at a few instructions -- the issuing thread
+    // shares its sub-partition with two softmax warps, and rebuilding two
+    // 64-bit descriptors per MMA made issue, not the tensor pipe, the limit.
     const uint32_t q_addr = tc::smem_u32(smem + Cfg::kQOff);
+    const uint64_t q_desc[2] = {tc::smem_desc_sw128(q_addr, 16, 1024),
+                                tc::smem_desc_sw128(q_addr + Cfg::kTileBytes, 16, 1024)};
+    const uint32_t k_addr0 = tc::smem_u32(smem + Cfg::kKOff);
+    const uint64_t k_desc[2] = {tc::smem_desc_sw128(k_addr0, 16, 1024),
+                                tc::smem_desc_sw128(k_addr0 + Cfg::kTileBytes, 16, 1024)};
+    const uint32_t v_addr0 = tc::smem_u32(smem + Cfg::kVOff);
+    const uint64_t v_desc[2] = {tc::smem_desc_sw128(v_addr0, Cfg::kBoxBytes, 1024),
+                                tc::smem_desc_sw128(v_addr0 + Cfg::kTileBytes, Cfg::kBoxBytes,
+                                                    1024)};
+    // K-major step kk: box kk/4, 32 bytes per 16 columns inside the box.
+    auto kstep = [](int kk) {
+      return static_cast<uint64_t>(((kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32) >> 4);
+    };
     // S block `buf` = Q_x K_j^T (K_j already landed); commit signals s_full[buf].
     auto qk_into = [&](int buf, int x, int j) {
-      const uint32_t k_addr = tc::smem_u32(smem + Cfg::kKOff + (j & 1) * Cfg::kTileBytes);
+      const uint64_t qd = q_desc[x], kd = k_desc[j & 1];
+      const uint32_t d_tmem = tmem + buf * kKeys;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk)
-        tc::umma_f16(tmem + buf * kKeys,
-                     kmajor_desc(q_addr + x * Cfg::kTileBytes, kk, Cfg::kBoxBytes),
-                     kmajor_desc(k_addr, kk, Cfg::kBoxBytes), Cfg::kIdescQK, kk != 0);
+        tc::umma_f16(d_tmem, qd + kstep(kk), kd + kstep(kk), Cfg::kIdescQK, kk != 0);
       tc::umma_commit(&bars->s_full[buf]);
       issued_any = true;
     };
@@ -257,14 +308,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // O_x += P (FP16 pairs in the first 64 columns of S block `buf`; 8
     // packed columns per 16 keys) * V_j.
     auto pv_from = [&](int buf, int x, int j, bool first) {
-      const uint32_t v_addr = tc::smem_u32(smem + Cfg::kVOff + (j & 1) * Cfg::kTileBytes);
+      const uint64_t vd = v_desc[j & 1];
+      const uint32_t d_tmem = tmem + Cfg::kColO0 + x * D;
+      const uint32_t p_tmem = tmem + buf * kKeys;
+      // V: N-major (D contiguous), 64-column boxes of 128 keys (16 KB
+      // apart); a 16-key step is two 8-row groups (2 KB).
+      tc::umma_f16_tmem_a(d_tmem, p_tmem, vd, Cfg::kIdescPV, first ? 0u : 1u);
 #pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk)
-        // V: N-major (D contiguous), 64-column boxes of 128 keys (16 KB
-        // apart); a 16-key step is two 8-row groups (2 KB).
-        tc::umma_f16_tmem_a(tmem + Cfg::kColO0 + x * D, tmem + buf * kKeys + kk * 8,
-                            tc::smem_desc_sw128(v_addr + kk * 2048, Cfg::kBoxBytes, 1024),
-                            Cfg::kIdescPV, !(first && kk == 0));
+      for (int kk = 1; kk < kKeys / 16; ++kk)
+        tc::umma_f16_tmem_a(d_tmem, p_tmem + kk * 8, vd + static_cast<uint64_t>(kk * 128),
+                            Cfg::kIdescPV, 1u);
       issued_any = true;
     };
     auto pv = [&](int x, int j) { pv_from(x, x, j, j == 0); };
@@ -380,25 +433,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // partial maxima / sums keep dependency chains short.
       float pm[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) pm[a] = s[a];
+      for (int a = 0; a < 8; ++a) pm[a] = fmax3(s[a], s[8 + a], s[16 + a]);
 #pragma unroll
-      for (int i = 8; i < kKeys; ++i) pm[i & 7] = fmaxf(pm[i & 7], s[i]);
-      const float mx = scale_log2 * fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                                          fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+      for (int i = 24; i < kKeys; i += 16) {
+#pragma unroll
+        for (int a = 0; a < 8; ++a) pm[a] = fmax3(pm[a], s[i + a], s[i + 8 + a]);
+      }
+      const float mx = scale_log2 * fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
+                                          fmaxf(pm[6], pm[7]));
       float alpha = 1.0f;
       if (mx > m_used + kRescaleThreshold) {
         alpha = (m_used == -INFINITY) ? 0.0f : exp2f(m_used - mx);
         m_used = mx;
         l *= alpha;
       }
-      // 2^(s*scale - m) for all 128 keys on the MUFU unit (ex2.approx,
-      // relative error ~2^-22, far below the FP16 rounding of P), eight
-      // independent partial sums.  Measured on B200, MUFU throughput is the
-      // softmax's limit; an FMA-pipe polynomial for part of the keys cost
-      // more issue slots than it saved.
-      // Scale-and-shift and the row sum on packed FP32 pairs (fma.rn.f32x2 /
-      // add.rn.f32x2: two IEEE FP32 operations per instruction), halving
-      // their issue slots next to the MUFU exponentials.
+      // 2^(s*scale - m) for the 128 keys: 80 on the MUFU unit (ex2.approx,
+      // relative error ~2^-22) and 48 (pairs 0, 3 and 6 of every 8) as an
+      // FMA-pipe polynomial (exp2_poly_x2), so that MUFU -- which two
+      // softmax warps share per sub-partition -- is no longer the only unit
+      // doing exponentials.  Both errors are far below the FP16 rounding of
+      // P.  Eight independent partial sums.  Scale-and-shift, the polynomial
+      // and the row sum run on packed FP32 pairs (fma.rn.f32x2 /
+      // add.rn.f32x2: two IEEE FP32 operations per instruction).
       uint64_t ps2[4] = {0, 0, 0, 0};
       const uint64_t scale2 = f32x2(scale_log2, scale_log2);
       const uint64_t shift2 = f32x2(-m_used, -m_used);
@@ -406,8 +462,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < kKeys / 2; ++i) {
         float x0, x1;
         split_f32x2(fma_f32x2(f32x2(s[2 * i], s[2 * i + 1]), scale2, shift2), x0, x1);
-        s[2 * i] = fast_exp2(x0);  // -inf -> 0
-        s[2 * i + 1] = fast_exp2(x1);
+        if ((i & 7) == 0 || (i & 7) == 3 || (i & 7) == 6) {
+          exp2_poly_x2(f32x2(fmaxf(x0, -120.0f), fmaxf(x1, -120.0f)), s[2 * i], s[2 * i + 1]);
+        } else {
+          s[2 * i] = fast_exp2(x0);  // -inf -> 0
+          s[2 * i + 1] = fast_exp2(x1);
+        }
         ps2[i & 3] = add_f32x2(ps2[i & 3], f32x2(s[2 * i], s[2 * i + 1]));
       }
       float ps[8];
@@ -460,18 +520,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t oa_col = tmem + lane_off + Cfg::kColO0;
         uint8_t* stage = smem + Cfg::kQOff + (warp - kSoftmaxWarp0) * 8192;
         const int y0 = qt0 * kRowsQ + quarter * 32;
-#pragma unroll 1
+        // All of this warp's TMEM loads are issued before one wait (each
+        // load waited for alone costs its full latency).
+        uint32_t oraw[2 * (D / 64)][32];
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tc::tmem_ld32_nowait(oa_col + x * (D / 2) + c * 32, oraw[2 * c]);
+          tc::tmem_ld32_nowait(oa_col + D + x * (D / 2) + c * 32, oraw[2 * c + 1]);
+        }
+#pragma unroll
+        for (int c = 0; c < 2 * (D / 64); ++c) tc::tmem_wait_ld32(oraw[c]);
+#pragma unroll
         for (int c = 0; c < D / 64; ++c) {
           const int col = x * (D / 2) + c * 32;
           float o[32];
-          tc::tmem_ld32(oa_col + col, o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= wa;
-          if (has_b) {
-            float ob[32];
-            tc::tmem_ld32(oa_col + D + col, ob);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = fmaf(ob[i], wb, o[i]);
+          for (int i = 0; i < 32; ++i) {
+            o[i] = __uint_as_float(oraw[2 * c][i]) * wa;
+            if (has_b) o[i] = fmaf(__uint_as_float(oraw[2 * c + 1][i]), wb, o[i]);
           }
           uint8_t* buf = stage + (c & 1) * 4096;
           if (lane == 0) tc::bulk_wait_read<1>();
@@ -499,15 +565,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // segments per store instruction.
       tc::tc_fence_after();
       const float inv = 1.0f / l;
-      uint8_t* stage = smem + Cfg::kQOff + (warp - kSoftmaxWarp0) * 8192;
+      // One 4 KB staging buffer per 32 columns (8 warps x D KB fits in the
+      // Q and K regions), so no store waits for an earlier one; all TMEM
+      // loads are issued before one wait.
+      uint8_t* stage = smem + Cfg::kQOff + (warp - kSoftmaxWarp0) * (D / 32) * 4096;
       const int y0 = (qt0 + x) * kRowsQ + quarter * 32;
-#pragma unroll 1
+      uint32_t oraw[D / 32][32];
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tc::tmem_ld32_nowait(o_col + c * 32, oraw[c]);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) tc::tmem_wait_ld32(oraw[c]);
+#pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         float o[32];
-        tc::tmem_ld32(o_col + c * 32, o);
-        uint8_t* buf = stage + (c & 1) * 4096;
-        if (lane == 0) tc::bulk_wait_read<1>();  // the store that used buf is done reading
-        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(oraw[c][i]);
+        uint8_t* buf = stage + c * 4096;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
           *reinterpret_cast<float4*>(buf + lane * 128 + ((k ^ (lane & 7)) * 16)) =

@@ -24,6 +24,8 @@
 // Every mbarrier wait is bounded (tc_common.cuh): a wait that gives up sets
 // the CTA's abort flag and the device watchdog word; the CTA then drains its
 // outstanding TMA loads and MMAs (again bounded), frees TMEM and exits.
+#include <algorithm>
+
 #include "gemm_simt.cuh"
 #include "tc_common.cuh"
 #include "tmap.cuh"
@@ -385,45 +387,59 @@ __global__ void __launch_bounds__(256)
 // Widest N remainder whose product the A-padding pass computes itself.
 constexpr int kPadDotMaxTail = 8;
 
+
 // pad_half_kernel for A (rows x cols into rows x pcol) that also computes the
 // narrow N remainder while each row is in registers: c[r][j] = sum over kk of
 // A[r][kk] * bt[j][kk] for j < n_tail <= kPadDotMaxTail, bt the K-major tail
-// strip of B (row stride pcol, zero past cols).  Products of two halves are
-// exact in FP32; each thread sums its groups in order, then warps and the
-// block in a fixed order, so results repeat bit for bit.  This replaces a
-// second full read of A by a skinny-N product after the GEMM.
-__global__ void __launch_bounds__(256)
+// strip of B (row stride pcol, zero past cols; a few KB, served from L1).
+// One warp per row, grid-stride over rows, kPadBatch 16-byte groups loaded
+// before any is stored, so every SM streams from the start (one 256-thread
+// CTA per row spent most of its time in launch and block reductions).
+// Products of two halves are exact in FP32; each lane sums its groups in
+// order, then a fixed xor tree, so results repeat bit for bit.  This replaces
+// a second full read of A by a skinny-N product after the GEMM.
+constexpr int kPadWarps = 8;
+constexpr int kPadBatch = 4;
+
+__global__ void __launch_bounds__(kPadWarps * 32)
     pad_half_tail_dot_kernel(const __half* __restrict__ src, int rows, int cols,
                              __half* __restrict__ dst, int pcol,
                              const __half* __restrict__ bt, int n_tail,
                              float* __restrict__ c, int ldc) {
-  __shared__ float part[8][kPadDotMaxTail];
   const int groups = pcol / 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const HalfRows in(src, rows, cols);
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  for (int r = blockIdx.x * kPadWarps + warp; r < rows; r += gridDim.x * kPadWarps) {
     uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
     float acc[kPadDotMaxTail];
 #pragma unroll
     for (int j = 0; j < kPadDotMaxTail; ++j) acc[j] = 0.0f;
-    for (int g = threadIdx.x; g < groups; g += blockDim.x) {
-      const uint4 av = g * 8 < cols ? in.group(r, g) : make_uint4(0, 0, 0, 0);
-      drow[g] = av;
-      const __half2* a2 = reinterpret_cast<const __half2*>(&av);
-      float2 af[4];
+    for (int g0 = lane; g0 < groups; g0 += 32 * kPadBatch) {
+      uint4 v[kPadBatch];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) af[i] = __half22float2(a2[i]);
+      for (int u = 0; u < kPadBatch; ++u) {
+        const int g = g0 + 32 * u;
+        v[u] = (g < groups && g * 8 < cols) ? in.group(r, g) : make_uint4(0, 0, 0, 0);
+      }
 #pragma unroll
-      for (int j = 0; j < kPadDotMaxTail; ++j) {
-        if (j < n_tail) {
-          const uint4 bv =
-              __ldg(reinterpret_cast<const uint4*>(bt + static_cast<size_t>(j) * pcol) + g);
-          const __half2* b2 = reinterpret_cast<const __half2*>(&bv);
+      for (int u = 0; u < kPadBatch; ++u) {
+        const int g = g0 + 32 * u;
+        if (g >= groups) break;
+        drow[g] = v[u];
+        const __half2* a2 = reinterpret_cast<const __half2*>(&v[u]);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float2 bf = __half22float2(b2[i]);
-            acc[j] = fmaf(af[i].x, bf.x, acc[j]);
-            acc[j] = fmaf(af[i].y, bf.y, acc[j]);
+        for (int j = 0; j < kPadDotMaxTail; ++j) {
+          if (j < n_tail) {
+            const uint4 bv =
+                __ldg(reinterpret_cast<const uint4*>(bt + static_cast<size_t>(j) * pcol) + g);
+            const __half2* b2 = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 af = __half22float2(a2[i]);
+              const float2 bf = __half22float2(b2[i]);
+              acc[j] = fmaf(af.x, bf.x, acc[j]);
+              acc[j] = fmaf(af.y, bf.y, acc[j]);
+            }
           }
         }
       }
@@ -431,19 +447,10 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int j = 0; j < kPadDotMaxTail; ++j) {
       if (j < n_tail) {
-        float v = acc[j];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-        if (lane == 0) part[warp][j] = v;
+        const float v = warp_sum(acc[j]);
+        if (lane == 0) c[static_cast<size_t>(r) * ldc + j] = v;
       }
     }
-    __syncthreads();
-    if (static_cast<int>(threadIdx.x) < n_tail) {
-      float v = 0.0f;
-      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) v += part[w][threadIdx.x];
-      c[static_cast<size_t>(r) * ldc + threadIdx.x] = v;
-    }
-    __syncthreads();
   }
 }
 
@@ -809,8 +816,9 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
     __half* dst = reinterpret_cast<__half*>(wsb);
     const int grid = m < 65535 ? m : 65535;
     if (tail_in_pad)
-      pad_half_tail_dot_kernel<<<grid, 256, 0, stream>>>(a, m, k, dst, kp, bt, n_tail,
-                                                         c + n_main, n);
+      pad_half_tail_dot_kernel<<<std::min((m + kPadWarps - 1) / kPadWarps, 8 * sm_count()),
+                                 kPadWarps * 32, 0, stream>>>(a, m, k, dst, kp, bt, n_tail,
+                                                              c + n_main, n);
     else
       pad_half_kernel<<<grid, 256, 0, stream>>>(a, m, k, dst, m, kp);
     a_use = dst;

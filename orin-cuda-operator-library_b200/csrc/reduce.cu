@@ -79,8 +79,13 @@ __global__ void __launch_bounds__(kReduceThreads)
   }
 }
 
-int reduce_grid(std::size_t n) {
-  const std::size_t vectors = n / 4 + 1;
+int reduce_grid(const float* input, std::size_t n) {
+  // Exactly the CTAs the aligned float4 body needs (the scalar head and tail
+  // ride along on the first threads), at least one.
+  const std::uintptr_t address = reinterpret_cast<std::uintptr_t>(input);
+  std::size_t head = ((16u - (address & 15u)) & 15u) / 4u;
+  if (head > n) head = n;
+  const std::size_t vectors = (n - head) / 4;
   const std::size_t span = static_cast<std::size_t>(kReduceThreads) * kUnroll;
   std::size_t blocks = (vectors + span - 1) / span;
   if (blocks > static_cast<std::size_t>(kReduceMaxCtas)) blocks = kReduceMaxCtas;
@@ -118,7 +123,7 @@ cudaError_t reduce_enqueue(const float* input, std::size_t n, double* partials,
 static int reduce_with_workspace(const float* input, std::size_t n,
                                  float* out_f32, double* out_f64,
                                  cudaStream_t stream) {
-  const int blocks = reduce_grid(n);
+  const int blocks = reduce_grid(input, n);
   void* workspace = nullptr;
   cudaError_t error = cudaMallocAsync(&workspace, blocks * sizeof(double), stream);
   if (error != cudaSuccess) return error;

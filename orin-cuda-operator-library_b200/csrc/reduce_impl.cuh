@@ -33,9 +33,9 @@ __device__ __forceinline__ double block_sum_fixed(double v) {
   return total;
 }
 
-// Number of partial-sum CTAs used for n elements on the current device
-// (at most kReduceMaxCtas).
-int reduce_grid(std::size_t n);
+// Number of partial-sum CTAs for n elements starting at input (at most
+// kReduceMaxCtas).
+int reduce_grid(const float* input, std::size_t n);
 
 // Enqueues the partial kernel (blocks CTAs, one FP64 partial each written to
 // partials[0..blocks)) and the fixed-order finalize kernel, which writes the

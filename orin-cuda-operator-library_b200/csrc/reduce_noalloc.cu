@@ -62,7 +62,7 @@ cudaError_t scratch_address(double** out) {
 extern "C" int opl_reduce_sum_f32_noalloc(const float* input, float* output,
                                           size_t n, opl_stream_t stream) {
   if (input == nullptr || output == nullptr || n == 0) return cudaErrorInvalidValue;
-  const int blocks = opl::reduce_grid(n);
+  const int blocks = opl::reduce_grid(input, n);
   double* scratch = nullptr;
   const cudaError_t error = opl::scratch_address(&scratch);
   if (error != cudaSuccess) return error;

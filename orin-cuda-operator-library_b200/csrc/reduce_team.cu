@@ -188,7 +188,7 @@ int opl_team_reduce_sum_f32(void* team_ptr, const float* input, float* output, s
     return cudaErrorInvalidValue;
   for (int r = 0; r < team->world; ++r)
     if (team->peers.peer[r] == nullptr) return cudaErrorInvalidValue;  // not connected
-  const int blocks = reduce_grid(n);
+  const int blocks = reduce_grid(input, n);
   void* workspace = nullptr;
   cudaError_t e = cudaMallocAsync(&workspace, blocks * sizeof(double), stream);
   if (e != cudaSuccess) return e;

@@ -26,9 +26,9 @@ __global__ void __launch_bounds__(kT4Threads)
   const int r0 = threadIdx.x >> 4;        // 0..15
   const int cols4 = cols >> 2;
   const int rows4 = rows >> 2;
-  // grid.y is capped at 65535: taller inputs loop over their row tiles.
-  for (long long tr = static_cast<long long>(blockIdx.y) * kT4; tr < rows;
-       tr += static_cast<long long>(gridDim.y) * kT4) {
+  // Row tiles past grid.y's limit of 65535 continue in grid.z.
+  const long long tr = (static_cast<long long>(blockIdx.z) * gridDim.y + blockIdx.y) * kT4;
+  if (tr >= rows) return;
   const int tile_row = static_cast<int>(tr);  // input row origin
 
   // Load: 64 rows x 16 float4, four passes of 16 rows.
@@ -69,8 +69,6 @@ __global__ void __launch_bounds__(kT4Threads)
                 y);
     }
   }
-  __syncthreads();  // the tile is refilled by the next row tile
-  }
 }
 
 constexpr int kT1 = 32;
@@ -81,9 +79,9 @@ __global__ void __launch_bounds__(kT1 * kT1Rows)
                             float* __restrict__ output, int rows, int cols) {
   __shared__ float tile[kT1][kT1 + 1];
   const int x = blockIdx.x * kT1 + threadIdx.x;
-  // grid.y is capped at 65535: taller inputs loop over their row tiles.
-  for (long long r0l = static_cast<long long>(blockIdx.y) * kT1; r0l < rows;
-       r0l += static_cast<long long>(gridDim.y) * kT1) {
+  // Row tiles past grid.y's limit of 65535 continue in grid.z.
+  const long long r0l = (static_cast<long long>(blockIdx.z) * gridDim.y + blockIdx.y) * kT1;
+  if (r0l >= rows) return;
   const int row0 = static_cast<int>(r0l);
   const int y = row0 + threadIdx.y;
 #pragma unroll
@@ -101,8 +99,13 @@ __global__ void __launch_bounds__(kT1 * kT1Rows)
       st_stream(output + static_cast<std::size_t>(oy + k) * rows + ox,
                 tile[threadIdx.x][threadIdx.y + k]);
   }
-  __syncthreads();  // the tile is refilled by the next row tile
-  }
+}
+
+// Column tiles on x, row tiles on y (at most 65535) and, beyond that, z.
+dim3 tile_grid(int rows, int cols, int tile) {
+  const int row_tiles = (rows + tile - 1) / tile;
+  const int y = std::min(row_tiles, 65535);
+  return dim3((cols + tile - 1) / tile, y, (row_tiles + y - 1) / y);
 }
 
 }  // namespace opl
@@ -113,13 +116,11 @@ extern "C" int opl_transpose_f32(const float* input, float* output, int rows,
   if (input == nullptr || output == nullptr || rows <= 0 || cols <= 0)
     return cudaErrorInvalidValue;
   if (rows % 4 == 0 && cols % 4 == 0 && aligned16(input) && aligned16(output)) {
-    const dim3 grid((cols + kT4 - 1) / kT4,
-                    std::min((rows + kT4 - 1) / kT4, 65535));
+    const dim3 grid = tile_grid(rows, cols, kT4);
     transpose_vec4_kernel<<<grid, kT4Threads, 0, stream>>>(input, output, rows,
                                                             cols);
   } else {
-    const dim3 grid((cols + kT1 - 1) / kT1,
-                    std::min((rows + kT1 - 1) / kT1, 65535));
+    const dim3 grid = tile_grid(rows, cols, kT1);
     transpose_scalar_kernel<<<grid, dim3(kT1, kT1Rows), 0, stream>>>(
         input, output, rows, cols);
   }
