@@ -360,96 +360,119 @@ struct HalfRows {
   }
 };
 
-// Zero-padded copy of a rows x cols FP16 matrix (any 2-byte-aligned base,
-// any row stride) into a prow x pcol buffer (pcol a multiple of 8, so every row
-// starts 16-byte aligned for TMA), 128-bit loads and stores.  With
-// tail != nullptr it also gathers columns [tail_col0, tail_col0 + n_tail)
-// (n_tail <= blockDim.x) into the K-major strip tail[j][r] (row stride
-// tail_ld; zero for r >= rows).
-__global__ void __launch_bounds__(256)
-    pad_half_kernel(const __half* __restrict__ src, int rows, int cols,
-                    __half* __restrict__ dst, int prow, int pcol,
-                    __half* __restrict__ tail = nullptr, int tail_col0 = 0, int n_tail = 0,
-                    int tail_ld = 0) {
-  const int groups = pcol / 8;
-  const HalfRows in(src, rows, cols);
-  for (int r = blockIdx.x; r < prow; r += gridDim.x) {
-    uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
-    for (int g = threadIdx.x; g < groups; g += blockDim.x)
-      drow[g] = (r < rows && g * 8 < cols) ? in.group(r, g) : make_uint4(0, 0, 0, 0);
-    if (tail != nullptr && static_cast<int>(threadIdx.x) < n_tail)
-      tail[static_cast<size_t>(threadIdx.x) * tail_ld + r] =
-          r < rows ? src[static_cast<size_t>(r) * cols + tail_col0 + threadIdx.x]
-                   : __float2half(0.0f);
-  }
-}
-
 // Widest N remainder whose product the A-padding pass computes itself.
 constexpr int kPadDotMaxTail = 8;
 
 
-// pad_half_kernel for A (rows x cols into rows x pcol) that also computes the
-// narrow N remainder while each row is in registers: c[r][j] = sum over kk of
-// A[r][kk] * bt[j][kk] for j < n_tail <= kPadDotMaxTail, bt the K-major tail
-// strip of B (row stride pcol, zero past cols; a few KB, served from L1).
-// One warp per row, grid-stride over rows, kPadBatch 16-byte groups loaded
-// before any is stored, so every SM streams from the start (one 256-thread
-// CTA per row spent most of its time in launch and block reductions).
-// Products of two halves are exact in FP32; each lane sums its groups in
-// order, then a fixed xor tree, so results repeat bit for bit.  This replaces
-// a second full read of A by a skinny-N product after the GEMM.
-constexpr int kPadWarps = 8;
-constexpr int kPadBatch = 4;
+// One zero-padded row-major FP16 matrix of the padding pass: src is rows x
+// cols at any 2-byte-aligned base, dst is prow x pcol (pcol a multiple of 8).
+struct PadJob {
+  const __half* src;
+  int rows, cols;
+  __half* dst;
+  int prow, pcol;
+};
 
-__global__ void __launch_bounds__(kPadWarps * 32)
-    pad_half_tail_dot_kernel(const __half* __restrict__ src, int rows, int cols,
-                             __half* __restrict__ dst, int pcol,
-                             const __half* __restrict__ bt, int n_tail,
-                             float* __restrict__ c, int ldc) {
-  const int groups = pcol / 8;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const HalfRows in(src, rows, cols);
-  for (int r = blockIdx.x * kPadWarps + warp; r < rows; r += gridDim.x * kPadWarps) {
-    uint4* drow = reinterpret_cast<uint4*>(dst + static_cast<size_t>(r) * pcol);
-    float acc[kPadDotMaxTail];
+// Both operands' padded copies in ONE launch, one CTA per destination row
+// (job 0's rows first, then job 1's).  Within a warp, lane l writes group
+// g0 + l (8 halves = 16 bytes) of the row: it loads the one aligned 16-byte
+// word under its group's start and takes the next word from lane l + 1 by
+// shuffle (lane 31 loads one more), then shifts by the row's start offset --
+// one 128-bit load and one 128-bit store per 16 bytes, no division (a
+// thread-per-group grid with a 64-bit row division ran at 4.1 TB/s, this
+// layout at 4.5 TB/s (5.1 TB/s with two CTAs per row, which the CTA-wide
+// remainder dot below rules out; 512 threads per row: 4.0 TB/s); an aligned
+// copy of the same bytes runs at 5.7 TB/s).
+// With n_tail > 0, job 1's rows (A) also compute the narrow N remainder
+// c[r][j] = sum over kk of A[r][kk] * bt[j][kk], j < n_tail <= kPadDotMaxTail,
+// bt the K-major tail strip of B (row stride pcol, zero past cols; a few KB,
+// served from L1): products of two halves are exact in FP32; each thread sums
+// its groups in order, then warps (xor tree) and the CTA's warps in a fixed
+// order, so results repeat bit for bit.
+constexpr int kPadThreads = 256;
+
+__global__ void __launch_bounds__(kPadThreads)
+    pad_rows_kernel(PadJob j0, PadJob j1, const __half* __restrict__ bt, int n_tail,
+                    float* __restrict__ c, int ldc) {
+  __shared__ float part[kPadThreads / 32][kPadDotMaxTail];
+  const bool second = static_cast<int>(blockIdx.x) >= j0.prow;
+  const PadJob& job = second ? j1 : j0;
+  const int r = second ? static_cast<int>(blockIdx.x) - j0.prow : static_cast<int>(blockIdx.x);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int groups = job.pcol / 8;
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(job.src);
+  const uint4* src4 = reinterpret_cast<const uint4*>(addr & ~uintptr_t(15));
+  const size_t lead = (addr & 15u) >> 1;
+  const size_t total = (lead + static_cast<size_t>(job.rows) * job.cols + 7) / 8;
+  const size_t row_h = lead + static_cast<size_t>(r) * job.cols;
+  const int o = static_cast<int>(row_h & 7);
+  const bool dot = second && n_tail > 0;
+  float acc[kPadDotMaxTail];
 #pragma unroll
-    for (int j = 0; j < kPadDotMaxTail; ++j) acc[j] = 0.0f;
-    for (int g0 = lane; g0 < groups; g0 += 32 * kPadBatch) {
-      uint4 v[kPadBatch];
+  for (int t = 0; t < kPadDotMaxTail; ++t) acc[t] = 0.0f;
+  uint4* drow = reinterpret_cast<uint4*>(job.dst + static_cast<size_t>(r) * job.pcol);
+  for (int g0 = warp * 32; g0 < groups; g0 += kPadThreads) {
+    const int g = g0 + lane;
+    uint4 out = make_uint4(0, 0, 0, 0);
+    if (r < job.rows && g0 * 8 < job.cols) {  // warp-uniform
+      const size_t c0 = (row_h + static_cast<size_t>(g) * 8) >> 3;
+      const uint4 lo = c0 < total ? __ldg(src4 + c0) : make_uint4(0, 0, 0, 0);
+      uint4 extra = make_uint4(0, 0, 0, 0);
+      if (lane == 31 && c0 + 1 < total) extra = __ldg(src4 + c0 + 1);
+      uint4 hi;
+      hi.x = __shfl_down_sync(kFullMask, lo.x, 1);
+      hi.y = __shfl_down_sync(kFullMask, lo.y, 1);
+      hi.z = __shfl_down_sync(kFullMask, lo.z, 1);
+      hi.w = __shfl_down_sync(kFullMask, lo.w, 1);
+      if (lane == 31) hi = extra;
+      const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      out = halves_at(w, o);
+      const int valid = job.cols - g * 8;  // halves of this group inside the row
+      if (valid < 8) {
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
-      for (int u = 0; u < kPadBatch; ++u) {
-        const int g = g0 + 32 * u;
-        v[u] = (g < groups && g * 8 < cols) ? in.group(r, g) : make_uint4(0, 0, 0, 0);
+        for (int i = 0; i < 4; ++i) {
+          if (2 * i >= valid) ow[i] = 0;
+          else if (2 * i + 1 >= valid) ow[i] &= 0xffffu;
+        }
       }
+    }
+    if (g < groups) {
+      drow[g] = out;
+      if (dot) {
+        const __half2* a2 = reinterpret_cast<const __half2*>(&out);
 #pragma unroll
-      for (int u = 0; u < kPadBatch; ++u) {
-        const int g = g0 + 32 * u;
-        if (g >= groups) break;
-        drow[g] = v[u];
-        const __half2* a2 = reinterpret_cast<const __half2*>(&v[u]);
-#pragma unroll
-        for (int j = 0; j < kPadDotMaxTail; ++j) {
-          if (j < n_tail) {
+        for (int t = 0; t < kPadDotMaxTail; ++t) {
+          if (t < n_tail) {
             const uint4 bv =
-                __ldg(reinterpret_cast<const uint4*>(bt + static_cast<size_t>(j) * pcol) + g);
+                __ldg(reinterpret_cast<const uint4*>(bt + static_cast<size_t>(t) * job.pcol) + g);
             const __half2* b2 = reinterpret_cast<const __half2*>(&bv);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const float2 af = __half22float2(a2[i]);
               const float2 bf = __half22float2(b2[i]);
-              acc[j] = fmaf(af.x, bf.x, acc[j]);
-              acc[j] = fmaf(af.y, bf.y, acc[j]);
+              acc[t] = fmaf(af.x, bf.x, acc[t]);
+              acc[t] = fmaf(af.y, bf.y, acc[t]);
             }
           }
         }
       }
     }
+  }
+  if (dot) {  // CTA-uniform
 #pragma unroll
-    for (int j = 0; j < kPadDotMaxTail; ++j) {
-      if (j < n_tail) {
-        const float v = warp_sum(acc[j]);
-        if (lane == 0) c[static_cast<size_t>(r) * ldc + j] = v;
+    for (int t = 0; t < kPadDotMaxTail; ++t) {
+      if (t < n_tail) {
+        const float v = warp_sum(acc[t]);
+        if (lane == 0) part[warp][t] = v;
       }
+    }
+    __syncthreads();
+    if (static_cast<int>(threadIdx.x) < n_tail) {
+      float v = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kPadThreads / 32; ++w) v += part[w][threadIdx.x];
+      c[static_cast<size_t>(r) * ldc + threadIdx.x] = v;
     }
   }
 }
@@ -801,27 +824,30 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
   const __half* a_use = a;
   const __half* b_use = b;
   __half* bt = reinterpret_cast<__half*>(wsb + a_bytes + b_bytes);
-  if (!b_ok) {  // (with a split, the same pass gathers the tail columns)
-    __half* dst = reinterpret_cast<__half*>(wsb + a_bytes);
-    pad_half_kernel<<<kp < 65535 ? kp : 65535, 256, 0, stream>>>(
-        b, k, n, dst, kp, ldb_copy, split_n ? bt : nullptr, n_main, n_tail, kp);
-    b_use = dst;
-  } else if (split_n) {
+  // The remainder's K-major strip of B first (the A rows' dot reads it).
+  if (split_n)
     tail_columns_kernel<<<(kp + 255) / 256, 256, 0, stream>>>(b, k, n, n_main, n_tail, bt, kp);
-  }
-  // A narrow remainder is computed by the A-padding pass when there is one
-  // (after B's pass, which wrote the tail strip).
+  // A narrow remainder is computed by the padding pass when A is padded.
   const bool tail_in_pad = split_n && !a_ok && n_tail <= kPadDotMaxTail;
+  // Padded copies (B's rows first, then A's) in one launch.
+  PadJob jobs[2];
+  int n_jobs = 0;
+  if (!b_ok) {
+    __half* dst = reinterpret_cast<__half*>(wsb + a_bytes);
+    jobs[n_jobs++] = PadJob{b, k, n, dst, kp, ldb_copy};
+    b_use = dst;
+  }
   if (!a_ok) {
     __half* dst = reinterpret_cast<__half*>(wsb);
-    const int grid = m < 65535 ? m : 65535;
-    if (tail_in_pad)
-      pad_half_tail_dot_kernel<<<std::min((m + kPadWarps - 1) / kPadWarps, 8 * sm_count()),
-                                 kPadWarps * 32, 0, stream>>>(a, m, k, dst, kp, bt, n_tail,
-                                                              c + n_main, n);
-    else
-      pad_half_kernel<<<grid, 256, 0, stream>>>(a, m, k, dst, m, kp);
+    jobs[n_jobs++] = PadJob{a, m, k, dst, m, kp};
     a_use = dst;
+  }
+  if (n_jobs == 1) jobs[1] = jobs[0], jobs[0].prow = 0;  // the single job runs as job 1
+  if (n_jobs > 0) {
+    // (a row count beyond grid.x's limit fails to launch; the error is returned)
+    const long long rows = static_cast<long long>(jobs[0].prow) + jobs[1].prow;
+    pad_rows_kernel<<<static_cast<unsigned>(rows), kPadThreads, 0, stream>>>(
+        jobs[0], jobs[1], bt, tail_in_pad ? n_tail : 0, c + n_main, n);
   }
   e = cudaGetLastError();
   const int lda = a_ok ? k : kp;
