@@ -60,6 +60,8 @@ struct Barriers {
   int abort;
 };
 
+constexpr int kPairBM = 256;  // tile height of the CTA-pair kernel
+
 // Work units: tiles [0, tiles_full) whole; each remaining tail tile as two
 // K halves (2 units), so the last wave is two half-length passes instead of
 // one mostly idle full one.  Split units add into C (zeroed beforehand).
@@ -281,22 +283,56 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Zeroes the C tiles [tiles_full, tiles) that the GEMM will build from two
 // K halves added together (0 + a + b is the same in either order, so the
 // result stays deterministic).  One CTA per tile.
+// Zeroes row slice `slice` (BM/16 rows, one column per thread, kBN threads)
+// of tail tile `tail_index` of the tile grid (m, n, k, grid_ctas, group_m).
+template <int BM>
+__device__ __forceinline__ void zero_tail_slice(float* __restrict__ c, int m, int n, int k,
+                                                int ldc, int grid_ctas, int group_m,
+                                                int tail_index, int slice) {
+  TileGridT<BM> grid;
+  grid.group_m = group_m;
+  grid.init(m, n, k, grid_ctas, true);
+  int mb, nb;
+  grid.coords(grid.tiles_full + tail_index, mb, nb);
+  const int col = nb * kBN + threadIdx.x;
+  if (col >= n) return;
+  const int row0 = mb * BM + slice * (BM / 16);
+  const int row_end = min(m, row0 + BM / 16);
+#pragma unroll 8
+  for (int row = row0; row < row_end; ++row) c[static_cast<size_t>(row) * ldc + col] = 0.0f;
+}
+
 template <int BM>
 __global__ void __launch_bounds__(256)
     zero_tail_tiles_kernel(float* __restrict__ c, int m, int n, int k, int ldc,
                            int grid_ctas, int group_m) {
   // blockIdx.x: tail tile; blockIdx.y: its BM/16-row slice (16 per tile).
-  TileGridT<BM> grid;
-  grid.group_m = group_m;
-  grid.init(m, n, k, grid_ctas, true);
-  int mb, nb;
-  grid.coords(grid.tiles_full + blockIdx.x, mb, nb);
-  const int col = nb * kBN + threadIdx.x;  // kBN == blockDim.x
-  if (col >= n) return;
-  const int row0 = mb * BM + blockIdx.y * (BM / 16);
-  const int row_end = min(m, row0 + BM / 16);
-#pragma unroll 8
-  for (int row = row0; row < row_end; ++row) c[static_cast<size_t>(row) * ldc + col] = 0.0f;
+  zero_tail_slice<BM>(c, m, n, k, ldc, grid_ctas, group_m, blockIdx.x, blockIdx.y);
+}
+
+// The CTA-pair kernel's work split for C[m, n] over k: pairs in the grid
+// and, when the last wave is split into K halves, how many tail tiles must be
+// zeroed first (0 otherwise).  One place decides it, so a caller that zeroes
+// the tail inside its own launch agrees with launch_gemm_tc.
+struct PairPlan {
+  bool use_pair = false;
+  int pairs = 0, tail = 0, group_m = kGroupM;
+  bool split_tail = false;
+};
+
+PairPlan pair_plan(int m, int n, int k) {
+  PairPlan p;
+  p.use_pair = m >= kPairBM && n >= kBN && sm_count() >= 2;
+  if (!p.use_pair) return p;
+  const int k_blocks = (k + kBK - 1) / kBK;
+  const long long tiles =
+      static_cast<long long>((m + kPairBM - 1) / kPairBM) * ((n + kBN - 1) / kBN);
+  const int max_pairs = sm_count() / 2;
+  p.pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
+  const int tail = static_cast<int>(tiles % p.pairs);
+  p.split_tail = tiles > p.pairs && tail != 0 && 2 * tail <= p.pairs && k_blocks >= 8;
+  p.tail = p.split_tail ? tail : 0;
+  return p;
 }
 
 // Eight halves starting at half `o` (0..7) of the 16 halves in w[0..7]
@@ -389,12 +425,27 @@ struct PadJob {
 // served from L1): products of two halves are exact in FP32; each thread sums
 // its groups in order, then warps (xor tree) and the CTA's warps in a fixed
 // order, so results repeat bit for bit.
+// The same launch also zeroes the CTA-pair GEMM's split tail tiles (16 CTAs
+// per tile after the rows), which would otherwise take a launch of its own.
 constexpr int kPadThreads = 256;
+static_assert(kPadThreads == kBN, "tail zeroing writes one column per thread");
+
+struct TailZeroJob {
+  float* c;
+  int m, n, k, ldc, pairs, group_m, tail;  // tail == 0: nothing to zero
+};
 
 __global__ void __launch_bounds__(kPadThreads)
     pad_rows_kernel(PadJob j0, PadJob j1, const __half* __restrict__ bt, int n_tail,
-                    float* __restrict__ c, int ldc) {
+                    float* __restrict__ c, int ldc, TailZeroJob zero) {
   __shared__ float part[kPadThreads / 32][kPadDotMaxTail];
+  const int rows_total = j0.prow + j1.prow;
+  if (static_cast<int>(blockIdx.x) >= rows_total) {
+    const int z = static_cast<int>(blockIdx.x) - rows_total;
+    zero_tail_slice<kPairBM>(zero.c, zero.m, zero.n, zero.k, zero.ldc, zero.pairs,
+                             zero.group_m, z >> 4, z & 15);
+    return;
+  }
   const bool second = static_cast<int>(blockIdx.x) >= j0.prow;
   const PadJob& job = second ? j1 : j0;
   const int r = second ? static_cast<int>(blockIdx.x) - j0.prow : static_cast<int>(blockIdx.x);
@@ -494,7 +545,6 @@ __global__ void __launch_bounds__(kPadThreads)
 //            on the leader's "tmem_empty" barrier.
 // A cluster barrier after set-up and before exit keeps each CTA's barriers
 // and TMEM alive while its partner may still use them.
-constexpr int kPairBM = 256;
 constexpr int kPairStages = 6;
 constexpr int kPairABytes = 128 * kBK * 2;   // 16 KB: this CTA's 128 rows of A
 constexpr int kPairBBytes = 2 * kBBoxBytes;  // 16 KB: this CTA's 128 columns of B
@@ -701,8 +751,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tc::tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
+// tail_prezeroed: the caller already zeroed the pair plan's tail tiles.
 cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, int n,
-                           int k, int lda, int ldb, int ldc, cudaStream_t stream) {
+                           int k, int lda, int ldb, int ldc, cudaStream_t stream,
+                           bool tail_prezeroed = false) {
   CUtensorMap map_a, map_b;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
@@ -721,22 +773,19 @@ cudaError_t launch_gemm_tc(const __half* a, const __half* b, float* c, int m, in
     if (e != cudaSuccess) return e;
   }
   const int k_blocks = (k + kBK - 1) / kBK;
-  if (m >= kPairBM && n >= kBN && sm_count() >= 2) {
+  const PairPlan plan = pair_plan(m, n, k);
+  if (plan.use_pair) {
     // CTA pairs: 256 x 256 tiles, one pair per two SMs.
-    const int group_m = kGroupM;
+    const int group_m = plan.group_m;
+    const int pairs = plan.pairs;
+    const bool split_tail = plan.split_tail;
     cudaError_t e = cudaFuncSetAttribute(gemm_tc_pair_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(kPairSmemBytes));
     if (e != cudaSuccess) return e;
-    const long long tiles =
-        static_cast<long long>((m + kPairBM - 1) / kPairBM) * ((n + kBN - 1) / kBN);
-    const int max_pairs = sm_count() / 2;
-    const int pairs = static_cast<int>(tiles < max_pairs ? tiles : max_pairs);
-    const int tail = static_cast<int>(tiles % pairs);
-    const bool split_tail = tiles > pairs && tail != 0 && 2 * tail <= pairs && k_blocks >= 8;
-    if (split_tail) {
-      zero_tail_tiles_kernel<kPairBM><<<dim3(tail, 16), kBN, 0, stream>>>(c, m, n, k, ldc,
-                                                                          pairs, group_m);
+    if (split_tail && !tail_prezeroed) {
+      zero_tail_tiles_kernel<kPairBM><<<dim3(plan.tail, 16), kBN, 0, stream>>>(
+          c, m, n, k, ldc, pairs, group_m);
       e = cudaGetLastError();
       if (e != cudaSuccess) return e;
     }
@@ -843,16 +892,23 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
     a_use = dst;
   }
   if (n_jobs == 1) jobs[1] = jobs[0], jobs[0].prow = 0;  // the single job runs as job 1
+  // The GEMM's split tail tiles are zeroed by the same launch.
+  const PairPlan plan = pair_plan(m, n_main, kp);
+  const TailZeroJob zero{c, m, n_main, kp, n, plan.pairs, plan.group_m, plan.tail};
+  bool tail_zeroed = false;
   if (n_jobs > 0) {
-    // (a row count beyond grid.x's limit fails to launch; the error is returned)
-    const long long rows = static_cast<long long>(jobs[0].prow) + jobs[1].prow;
-    pad_rows_kernel<<<static_cast<unsigned>(rows), kPadThreads, 0, stream>>>(
-        jobs[0], jobs[1], bt, tail_in_pad ? n_tail : 0, c + n_main, n);
+    // (a block count beyond grid.x's limit fails to launch; the error is returned)
+    const long long blocks =
+        static_cast<long long>(jobs[0].prow) + jobs[1].prow + 16LL * zero.tail;
+    pad_rows_kernel<<<static_cast<unsigned>(blocks), kPadThreads, 0, stream>>>(
+        jobs[0], jobs[1], bt, tail_in_pad ? n_tail : 0, c + n_main, n, zero);
+    tail_zeroed = true;
   }
   e = cudaGetLastError();
   const int lda = a_ok ? k : kp;
   const int ldb = b_ok ? n : ldb_copy;
-  if (e == cudaSuccess) e = launch_gemm_tc(a_use, b_use, c, m, n_main, kp, lda, ldb, n, stream);
+  if (e == cudaSuccess)
+    e = launch_gemm_tc(a_use, b_use, c, m, n_main, kp, lda, ldb, n, stream, tail_zeroed);
   if (e == cudaSuccess && split_n && !tail_in_pad)
     e = gemm_small_n_tc(a_use, lda, bt, kp, c + n_main, n, m, n_tail, kp, stream);
   const cudaError_t f = cudaFreeAsync(ws, stream);
