@@ -524,11 +524,15 @@ def extras(args, dist, dev, peaks, only: set[str]):
     def want(name):
         return not only or name in only
 
-    def record(name, ms, work, peak, unit, world_units=1, sets=None, **extra):
+    def record(name, ms, work, peak, unit, world_units=1, sets=None, gpus=None, **extra):
+        # world_units: copies of `work` done in total (weak scaling: one per
+        # rank); gpus: GPUs sharing the rate (defaults to world_units; a
+        # strong-scaled config passes its total work and gpus=world).
         scale = 1e9 if unit == "GB/s" else 1e12
         rate = work * world_units / (ms * 1e-3) / scale
+        per_gpu = gpus if gpus is not None else world_units
         r = {"ms": round(ms, 5), "value": round(rate, 2), "unit": unit,
-             "frac": round(rate / world_units / peak, 4)}
+             "frac": round(rate / per_gpu / peak, 4)}
         if sets is not None:  # (input sets, bytes of one set)
             r["sets"] = [sets[0], round(sets[0] * sets[1] / 2**20)]
         r.update(extra)
@@ -763,7 +767,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
                       max(3, steps // 4), 2, dist, stream)
         flops = 2.0 * total_heads * d * s_len * (s_len + 1)
         record("attn_sharded_b8h32s4096d128_causal", ms, flops, tc, "TFLOP/s",
-               world_units=dist.world, heads_per_rank=mine)
+               gpus=dist.world, heads_per_rank=mine)
         # Parity on this rank's own shard: 2 heads x 10 sampled query rows
         # (first, last and spread rows), the oracle's exact per-row loop.
         torch.cuda.synchronize()
@@ -793,7 +797,7 @@ def extras(args, dist, dev, peaks, only: set[str]):
         ms = _measure(lambda i, h: lib.opl_gemm_f16(a.data_ptr(), b.data_ptr(), cc.data_ptr(),
                                                  m1 - m0, N, K, h), 3, 1, dist, stream)
         record("gemm_sharded_f16_16384", ms, 2.0 * M * N * K, tc, "TFLOP/s",
-               world_units=dist.world, rows_per_rank=m1 - m0)
+               gpus=dist.world, rows_per_rank=m1 - m0)
         # Parity on this rank's own rows: 16 sampled rows vs the FP64 product.
         torch.cuda.synchronize()
         idx = np.unique(np.linspace(0, m1 - m0 - 1, 16).astype(int))
@@ -1197,10 +1201,6 @@ def run_ours(args, dist) -> int:
     import operatorlib
 
     operatorlib.capi()  # fail loudly if the CUDA library is missing
-    if dist.world > 1:
-        # Communicator set-up lines (rank count, transport) in the log.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
     dist.init("nccl")
     dev = torch.device("cuda", dist.local_rank)
     torch.cuda.set_device(dev)
@@ -1362,6 +1362,12 @@ def run_profile(args) -> int:
 
 def main(argv=None) -> int:
     args = parse_args(argv)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        # NCCL communicator set-up lines (ranks, transports, NVLS) on stderr,
+        # so stdout keeps rank 0's JSON line last.  Set before torch loads NCCL.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.profile:
         return run_profile(args)
     dist = Dist()
