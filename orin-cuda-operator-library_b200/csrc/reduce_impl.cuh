@@ -9,11 +9,6 @@ constexpr int kReduceThreads = 256;
 // Upper bound on partial-sum CTAs (and so on FP64 partials per call).
 constexpr int kReduceMaxCtas = 4096;
 
-// Per-CTA FP64 partial sums of input[0..n) into partials[blockIdx.x]
-// (kReduceThreads threads; triggers programmatic dependent launch).
-__global__ void reduce_partials_kernel(const float* __restrict__ input, std::size_t n,
-                                       double* __restrict__ partials);
-
 // Launches reduce_partials_kernel with `blocks` CTAs on `stream`.
 cudaError_t reduce_partials_launch(const float* input, std::size_t n, double* partials,
                                    int blocks, cudaStream_t stream);
