@@ -50,7 +50,9 @@ GEMM_F16 = [(128, 128, 32), (16, 128, 32), (32, 32, 32), (37, 65, 71),  # ref te
             (1000, 4104, 512), (257, 300, 64), (200, 320, 96), (129, 513, 1000),
             (640, 769, 333),
             # ragged K with a remainder of <= 8 columns: computed in A's padding pass
-            (300, 262, 77), (200, 520, 45), (1000, 1033, 999)]
+            (300, 262, 77), (200, 520, 45), (1000, 1033, 999),
+            # larger padded products (both operands / a 1-column remainder)
+            (2048, 2304, 2050), (2304, 2561, 1999)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_F16)
@@ -259,7 +261,9 @@ def test_attention_f16_paired_tiles_sampled_heads(cuda, stream, b, h, s, d, caus
     (64, 72, 40, 1, 1), (300, 200, 136, 3, 3), (129, 257, 72, 5, 5), (1000, 1000, 1000, 7, 7),
     # only A misaligned, N a multiple of 256 plus <= 8: B stays in place and
     # the remainder columns are computed in A's padding pass
-    (300, 264, 64, 3, 0), (129, 520, 136, 1, 0)])
+    (300, 264, 64, 3, 0), (129, 520, 136, 1, 0),
+    # larger products with only A padded / only B padded
+    (2048, 2048, 2048, 3, 0), (2048, 2048, 2048, 0, 5)])
 def test_gemm_f16_misaligned_base_pointers(cuda, stream, m, n, k, offset, b_offset):
     """A starts `offset` halves and B `b_offset` halves into their allocations
     (2-byte aligned only): the zero-padded staging path must read them
@@ -279,7 +283,8 @@ def test_gemm_f16_misaligned_base_pointers(cuda, stream, m, n, k, offset, b_offs
     check_f16(c.cpu().numpy(), orc.gemm(a.astype(np.float32), b.astype(np.float32), threads=8))
 
 
-@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (4095, 4097, 4093), (2048, 2304, 1024), (1280, 2560, 1024)])
+@pytest.mark.parametrize("m,n,k", [(4096, 4096, 4096), (4095, 4097, 4093), (2048, 2304, 1024), (1280, 2560, 1024),
+                                   (2304, 2561, 1999)])
 def test_gemm_f16_deterministic(cuda, stream, m, n, k):
     """Shapes whose last wave is split into K halves (added into a zeroed C)
     still give bit-identical results run to run."""
