@@ -16,6 +16,7 @@ __global__ void __launch_bounds__(kBlock)
                           const float* __restrict__ weight,
                           float* __restrict__ output, int tokens, int hidden,
                           float epsilon) {
+  pdl_begin();
   constexpr int kWidth = RowElems<kVec>::kWidth;
   constexpr int kRowsPerBlock = kBlock / kGroup;
   __shared__ float scratch[kBlock / 32];
@@ -170,8 +171,10 @@ extern "C" int opl_rmsnorm_f32(const float* input, const float* weight,
   {                                                                             \
     const int rows_per_block = (B) / (G);                                       \
     const int blocks = (tokens + rows_per_block - 1) / rows_per_block;          \
-    rmsnorm_cached_kernel<G, B, I, V><<<blocks, B, 0, stream>>>(                \
-        input, weight, output, tokens, hidden, epsilon);                        \
+    const cudaError_t e = launch_pdl(rmsnorm_cached_kernel<G, B, I, V>,         \
+                                     dim3(blocks), dim3(B), stream, input,      \
+                                     weight, output, tokens, hidden, epsilon);  \
+    if (e != cudaSuccess) return e;                                             \
   }
   OPL_ROW_DISPATCH(shape, vec, OPL_RMSNORM_LAUNCH);
 #undef OPL_RMSNORM_LAUNCH

@@ -97,6 +97,7 @@ template <typename T, int kGroup, int kBlock, int kItems, bool kVec>
 __global__ void __launch_bounds__(kBlock)
     softmax16_kernel(const T* __restrict__ input, T* __restrict__ output, int rows, int cols) {
   constexpr int kW = kVec ? 8 : 1;
+  pdl_begin();
   __shared__ float scratch_max[kBlock / 32];
   __shared__ float scratch_sum[kBlock / 32];
   const int t = threadIdx.x % kGroup;
@@ -127,6 +128,7 @@ __global__ void __launch_bounds__(kBlock)
     rmsnorm16_kernel(const T* __restrict__ input, const T* __restrict__ weight,
                      T* __restrict__ output, int tokens, int hidden, float epsilon) {
   constexpr int kW = kVec ? 8 : 1;
+  pdl_begin();
   __shared__ float scratch[kBlock / 32];
   const int t = threadIdx.x % kGroup;
   const int row = blockIdx.x * (kBlock / kGroup) + threadIdx.x / kGroup;
@@ -266,8 +268,10 @@ int softmax16(const T* input, T* output, int rows, int cols, cudaStream_t stream
 #define OPL_SOFTMAX16(G, B, I, V)                                                         \
   {                                                                                       \
     const int per = (B) / (G);                                                            \
-    softmax16_kernel<T, G, B, I, V><<<(rows + per - 1) / per, B, 0, stream>>>(input, output, \
-                                                                             rows, cols); \
+    const cudaError_t e = launch_pdl(softmax16_kernel<T, G, B, I, V>,                   \
+                                     dim3((rows + per - 1) / per), dim3(B), stream, input,  \
+                                     output, rows, cols);                                   \
+    if (e != cudaSuccess) return e;                                                       \
   }
   OPL_ROW16_DISPATCH(s, vec, OPL_SOFTMAX16);
 #undef OPL_SOFTMAX16
@@ -289,8 +293,10 @@ int rmsnorm16(const T* input, const T* weight, T* output, int tokens, int hidden
 #define OPL_RMSNORM16(G, B, I, V)                                                         \
   {                                                                                       \
     const int per = (B) / (G);                                                            \
-    rmsnorm16_kernel<T, G, B, I, V><<<(tokens + per - 1) / per, B, 0, stream>>>(          \
-        input, weight, output, tokens, hidden, eps);                                      \
+    const cudaError_t e = launch_pdl(rmsnorm16_kernel<T, G, B, I, V>,                   \
+                                     dim3((tokens + per - 1) / per), dim3(B), stream,       \
+                                     input, weight, output, tokens, hidden, eps);           \
+    if (e != cudaSuccess) return e;                                                       \
   }
   OPL_ROW16_DISPATCH(s, vec, OPL_RMSNORM16);
 #undef OPL_RMSNORM16

@@ -16,6 +16,7 @@ template <int kGroup, int kBlock, int kItems, bool kVec>
 __global__ void __launch_bounds__(kBlock)
     softmax_cached_kernel(const float* __restrict__ input,
                           float* __restrict__ output, int rows, int cols) {
+  pdl_begin();
   constexpr int kWidth = RowElems<kVec>::kWidth;
   constexpr int kRowsPerBlock = kBlock / kGroup;
   __shared__ float scratch_max[kBlock / 32];
@@ -95,8 +96,10 @@ extern "C" int opl_softmax_f32(const float* input, float* output, int rows,
   {                                                                             \
     const int rows_per_block = (B) / (G);                                       \
     const int blocks = (rows + rows_per_block - 1) / rows_per_block;            \
-    softmax_cached_kernel<G, B, I, V><<<blocks, B, 0, stream>>>(input, output,  \
-                                                                rows, cols);    \
+    const cudaError_t e = launch_pdl(softmax_cached_kernel<G, B, I, V>,         \
+                                     dim3(blocks), dim3(B), stream, input,      \
+                                     output, rows, cols);                       \
+    if (e != cudaSuccess) return e;                                             \
   }
   OPL_ROW_DISPATCH(shape, vec, OPL_SOFTMAX_LAUNCH);
 #undef OPL_SOFTMAX_LAUNCH

@@ -77,6 +77,7 @@ constexpr int kT1Rows = 8;
 __global__ void __launch_bounds__(kT1 * kT1Rows)
     transpose_scalar_kernel(const float* __restrict__ input,
                             float* __restrict__ output, int rows, int cols) {
+  pdl_begin();
   __shared__ float tile[kT1][kT1 + 1];
   const int x = blockIdx.x * kT1 + threadIdx.x;
   // Row tiles past grid.y's limit of 65535 continue in grid.z.
@@ -121,8 +122,8 @@ extern "C" int opl_transpose_f32(const float* input, float* output, int rows,
                                                             cols);
   } else {
     const dim3 grid = tile_grid(rows, cols, kT1);
-    transpose_scalar_kernel<<<grid, dim3(kT1, kT1Rows), 0, stream>>>(
-        input, output, rows, cols);
+    return launch_pdl(transpose_scalar_kernel, grid, dim3(kT1, kT1Rows), stream, input,
+                      output, rows, cols);
   }
   return cudaGetLastError();
 }
