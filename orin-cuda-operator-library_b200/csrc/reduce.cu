@@ -49,6 +49,9 @@ ReduceSplit reduce_split(const float* input, std::size_t n) {
 
 __global__ void __launch_bounds__(kReduceThreads)
     reduce_partials_kernel(ReduceSplit in, double* __restrict__ partials) {
+  // Launched with programmatic dependent launch: scheduled while the
+  // previous kernel on the stream drains, global reads only after it is done.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // CTA b covers kUnroll consecutive CTA-widths of float4 per pass.
   const std::size_t span = static_cast<std::size_t>(kReduceThreads) * kUnroll;
   const std::size_t stride = static_cast<std::size_t>(gridDim.x) * span;
@@ -110,9 +113,8 @@ int reduce_grid(const float* input, std::size_t n) {
 
 cudaError_t reduce_partials_launch(const float* input, std::size_t n, double* partials,
                                    int blocks, cudaStream_t stream) {
-  reduce_partials_kernel<<<blocks, kReduceThreads, 0, stream>>>(reduce_split(input, n),
-                                                                 partials);
-  return cudaGetLastError();
+  return launch_pdl(reduce_partials_kernel, dim3(blocks), dim3(kReduceThreads), stream,
+                    reduce_split(input, n), partials);
 }
 
 cudaError_t reduce_enqueue(const float* input, std::size_t n, double* partials,
