@@ -1365,8 +1365,10 @@ def main(argv=None) -> int:
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         # NCCL communicator set-up lines (ranks, transports, NVLS) on stderr,
         # so stdout keeps rank 0's JSON line last.  Set before torch loads NCCL.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        # (An inherited NCCL_DEBUG of VERSION or WARN is raised to INFO.)
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"
+            os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.profile:
         return run_profile(args)
