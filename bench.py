@@ -1271,6 +1271,14 @@ def run_ours(args, dist) -> int:
         if ops:
             line["ops_fmt"] = OPS_FMT
             line["ops"] = compact_ops(ops, cpu_ops, par_all)
+            # Tensor-core configs that run for milliseconds back to back sit
+            # at the 1 kW power cap (sw_power_cap, SM clock ~1.43 GHz for the
+            # sharded attention): their fraction of the measured SUSTAINED
+            # bf16 GEMM peak, per GPU, beside the burst fraction in ops.
+            sus = peaks["bf16_tflops_sustained"]
+            line["frac_of_sustained_peak"] = {
+                name: round(r["value"] / dist.world / sus, 4) for name, r in ops.items()
+                if r["unit"] == "TFLOP/s" and ("sharded" in name or name == "gemm_f16_4096")}
         # Details that do not fit the one-line summary go to stderr.
         print(json.dumps({"bench_detail": {"ops": ops, "cpu_ops": cpu_ops,
                                            "parity": par_all,
