@@ -88,8 +88,7 @@ __global__ void __launch_bounds__(kReduceThreads)
                            float* __restrict__ output_f32,
                            double* __restrict__ output_f64) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  double v = 0.0;
-  for (int i = threadIdx.x; i < count; i += kReduceThreads) v += partials[i];
+  double v = sum_partials_strided(partials, count);
   v = block_sum_fixed(v);
   if (threadIdx.x == 0) {
     if (output_f32 != nullptr) *output_f32 = static_cast<float>(v);

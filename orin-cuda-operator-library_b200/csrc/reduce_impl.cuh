@@ -28,6 +28,24 @@ __device__ __forceinline__ double block_sum_fixed(double v) {
   return total;
 }
 
+// Sum of partials t, t + kReduceThreads, ... (in that order) for thread t,
+// count <= kReduceMaxCtas: all loads issued before the adds, so the thread
+// waits for one memory latency instead of one per partial.
+__device__ __forceinline__ double sum_partials_strided(const double* __restrict__ partials,
+                                                       int count) {
+  constexpr int kPer = kReduceMaxCtas / kReduceThreads;
+  double vals[kPer];
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int i = static_cast<int>(threadIdx.x) + u * kReduceThreads;
+    vals[u] = i < count ? partials[i] : 0.0;
+  }
+  double v = 0.0;
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) v += vals[u];
+  return v;
+}
+
 // Number of partial-sum CTAs for n elements starting at input (at most
 // kReduceMaxCtas).
 int reduce_grid(const float* input, std::size_t n);

@@ -71,8 +71,7 @@ __global__ void __launch_bounds__(kReduceThreads)
                                 float* __restrict__ output, int* watchdog) {
   __shared__ double local_total;
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  double v = 0.0;
-  for (int i = threadIdx.x; i < count; i += kReduceThreads) v += partials[i];
+  double v = sum_partials_strided(partials, count);
   v = block_sum_fixed(v);
   if (threadIdx.x == 0) local_total = v;
   __syncthreads();
