@@ -426,7 +426,7 @@ struct PadJob {
 // its groups in order, then warps (xor tree) and the CTA's warps in a fixed
 // order, so results repeat bit for bit.
 // The same launch also zeroes the CTA-pair GEMM's split tail tiles (16 CTAs
-// per tile after the rows), which would otherwise take a launch of its own.
+// per tile, before the rows), which would otherwise take a launch of its own.
 constexpr int kPadThreads = 256;
 static_assert(kPadThreads == kBN, "tail zeroing writes one column per thread");
 
@@ -439,16 +439,19 @@ __global__ void __launch_bounds__(kPadThreads)
     pad_rows_kernel(PadJob j0, PadJob j1, const __half* __restrict__ bt, int n_tail,
                     float* __restrict__ c, int ldc, TailZeroJob zero) {
   __shared__ float part[kPadThreads / 32][kPadDotMaxTail];
-  const int rows_total = j0.prow + j1.prow;
-  if (static_cast<int>(blockIdx.x) >= rows_total) {
-    const int z = static_cast<int>(blockIdx.x) - rows_total;
+  // The zeroing CTAs come first, so they run beside the rows rather than
+  // as a tail after them.
+  const int zero_ctas = 16 * zero.tail;
+  if (static_cast<int>(blockIdx.x) < zero_ctas) {
+    const int z = static_cast<int>(blockIdx.x);
     zero_tail_slice<kPairBM>(zero.c, zero.m, zero.n, zero.k, zero.ldc, zero.pairs,
                              zero.group_m, z >> 4, z & 15);
     return;
   }
-  const bool second = static_cast<int>(blockIdx.x) >= j0.prow;
+  const int item = static_cast<int>(blockIdx.x) - zero_ctas;
+  const bool second = item >= j0.prow;
   const PadJob& job = second ? j1 : j0;
-  const int r = second ? static_cast<int>(blockIdx.x) - j0.prow : static_cast<int>(blockIdx.x);
+  const int r = second ? item - j0.prow : item;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int groups = job.pcol / 8;
   const uintptr_t addr = reinterpret_cast<uintptr_t>(job.src);
