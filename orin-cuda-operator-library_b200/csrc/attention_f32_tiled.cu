@@ -15,8 +15,11 @@
 // Register-tile updates use packed fma.rn.f32x2 (two independent FP32 FMAs
 // per instruction, same rounding as fmaf).  Causal tiles past the diagonal
 // are skipped; the grid starts with the longest (bottom) query blocks.  When
-// (head, query block) units would leave SMs idle, the KV range is split across
-// CTAs and attention_combine_kernel merges the partial results.
+// (head, query block) units would leave SMs idle, one CTA per SM runs an
+// equal share of all KV tiles (balanced schedule) and
+// attention_combine_ranges_kernel merges the units split between CTAs.
+#include <algorithm>
+
 #include "attention_simt.cuh"
 
 namespace opl {
@@ -62,7 +65,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     attention_f32_tiled_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                const float* __restrict__ v, float* __restrict__ out,
                                int heads_total, int seq, int hd, int causal, float scale,
-                               int splits, float* __restrict__ part_o,
+                               int balanced, float* __restrict__ part_o,
                                float2* __restrict__ part_ml) {
   using Cfg = F32Cfg<D>;
   extern __shared__ __align__(16) float smem[];
@@ -72,16 +75,61 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* pt = vs + kBN * Cfg::kVPitch;           // [kBN][kPPitch]
 
   const int q_blocks = (seq + kBM - 1) / kBM;
-  const int sp = blockIdx.x % splits;
-  const int rest = blockIdx.x / splits;
+  const int tid = threadIdx.x;
+  const int tr = tid >> 4;
+  const int tc = tid & 15;
+  // Work units: unit u = (head u % heads_total, query block q_blocks - 1 -
+  // u / heads_total), longest (bottom) blocks first; a unit's work is its KV
+  // tiles.  balanced == 0: CTA = unit, all of its KV tiles.  balanced == 1:
+  // the units' KV tiles laid end to end are cut into gridDim.x
+  // equal ranges, one per CTA; a CTA runs every (unit, KV range) segment of
+  // its range, writing a unit it covers whole straight to `out` and a unit
+  // it covers in part (at most its first and last segments) to partial slot
+  // 2 blockIdx.x (first) or 2 blockIdx.x + 1 (last), which
+  // attention_combine_ranges_kernel merges.
+  const long long units = static_cast<long long>(heads_total) * q_blocks;
+  auto unit_tiles = [&](long long u) {
+    const int qb_u = q_blocks - 1 - static_cast<int>(u / heads_total);
+    const int last = min(qb_u * kBM + kBM, seq) - 1;
+    return ((causal ? last + 1 : seq) + kBN - 1) / kBN;
+  };
+  long long unit, pos, range_end, unit_start = 0;
+  if (!balanced) {
+    unit = blockIdx.x;
+    pos = 0;
+    range_end = 0;  // unused
+  } else {
+    // Units come in groups of heads_total with equal tile counts (one query
+    // block each), so the prefix sums walk q_blocks groups, not all units.
+    long long total = 0;
+    for (int g = 0; g < q_blocks; ++g) total += static_cast<long long>(heads_total) *
+                                                unit_tiles(static_cast<long long>(g) * heads_total);
+    pos = total * blockIdx.x / gridDim.x;
+    range_end = total * (blockIdx.x + 1) / gridDim.x;
+    unit = 0;
+    for (int g = 0; g < q_blocks; ++g) {
+      const long long t = unit_tiles(static_cast<long long>(g) * heads_total);
+      if (unit_start + t * heads_total <= pos) {
+        unit_start += t * heads_total;
+        unit += heads_total;
+        continue;
+      }
+      const long long in_group = (pos - unit_start) / t;
+      unit += in_group;
+      unit_start += in_group * t;
+      break;
+    }
+  }
+  bool first_segment = true;
+  for (;;) {
+  if (balanced && pos >= range_end) break;
+  const int rest = static_cast<int>(unit);
   const int bh = rest % heads_total;
   const int qb = q_blocks - 1 - rest / heads_total;
   const int q0 = qb * kBM;
   // hd <= D: the caller's head_dim; columns hd .. D-1 are zero padding.
   const size_t base = static_cast<size_t>(bh) * seq * hd;
-  const int tid = threadIdx.x;
-  const int tr = tid >> 4;
-  const int tc = tid & 15;
+  __syncthreads();  // the previous segment is done with the shared tiles
 
   // Q tile -> d-major shared copy (rows past S are zero).
   for (int idx = tid; idx < kBM * (D / 4); idx += kThreads) {
@@ -108,11 +156,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int q_last = min(q0 + kBM, seq) - 1;
   const int key_total = causal ? q_last + 1 : seq;
-  // This CTA's share of the KV tiles (all of them when splits == 1).
+  // This CTA's share of the unit's KV tiles (all of them when not balanced).
   const int kv_tiles = (key_total + kBN - 1) / kBN;
-  const int chunk = (kv_tiles + splits - 1) / splits;
-  const int key_begin = min(sp * chunk, kv_tiles) * kBN;
-  const int key_end = min(min((sp + 1) * chunk, kv_tiles) * kBN, key_total);
+  int tile_lo = 0, tile_hi = kv_tiles;
+  if (balanced) {
+    tile_lo = static_cast<int>(pos - unit_start);
+    tile_hi = static_cast<int>(min(range_end - unit_start, static_cast<long long>(kv_tiles)));
+  }
+  const int key_begin = tile_lo * kBN;
+  const int key_end = min(tile_hi * kBN, key_total);
+  // Partial result slot of this CTA's first / last segment when it covers the
+  // unit in part; -1: the whole unit, written to out.
+  long long part_slot = -1;
+  if (balanced && (tile_lo > 0 || tile_hi < kv_tiles))
+    part_slot = 2LL * blockIdx.x + (first_segment ? 0 : 1);
   for (int k0 = key_begin; k0 < key_end; k0 += kBN) {
     __syncthreads();  // previous tile consumed (and Q written on the first pass)
     for (int idx = tid; idx < kBN * (D / 4); idx += kThreads) {
@@ -221,16 +278,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if (splits > 1) {
-    // Partial result of this KV chunk: unnormalised O with its (m, l);
-    // attention_combine_kernel merges the chunks.  An empty chunk leaves
-    // m = -inf, l = 0, O = 0.
-    const size_t slice = static_cast<size_t>(heads_total) * seq;
+  if (part_slot >= 0) {
+    // Partial result of this KV range: unnormalised O with its (m, l);
+    // attention_combine_ranges_kernel merges the parts.
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int row = q0 + tr * 8 + i;
       if (row >= seq) continue;
-      const size_t r_index = static_cast<size_t>(sp) * slice + static_cast<size_t>(bh) * seq + row;
+      const size_t r_index = static_cast<size_t>(part_slot) * kBM + (row - q0);
       if (tc == 0) part_ml[r_index] = make_float2(m_run[i], l_run[i]);
       float* orow = part_o + r_index * hd + tc * Cfg::kCols;
 #pragma unroll
@@ -242,8 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(orow + 2 * c) = make_float4(a0, a1, b0, b1);
       }
     }
-    return;
-  }
+  } else {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int row = q0 + tr * 8 + i;
@@ -260,36 +314,97 @@ __global__ void __launch_bounds__(kThreads, 1)
             make_float4(a0 * inv, a1 * inv, b0 * inv, b1 * inv);
     }
   }
+  }
+  if (!balanced) break;
+  pos = unit_start + tile_hi;
+  unit_start += kv_tiles;
+  ++unit;
+  first_segment = false;
+  }
 }
 
 }  // namespace
 
-// Merges split-KV partial results: per (head, row), m = max_s m_s,
-// l = sum_s l_s e^(m_s - m), O = sum_s O_s e^(m_s - m) / l, splits added in
-// order s = 0, 1, ... (deterministic).  One warp per row, D/32 floats per
-// lane.  `log2_domain` selects 2^x (tensor-core kernel) instead of e^x.
+// Merges the partial results of the balanced schedule: for every unit that
+// more than one CTA covered, per row, m = max over its parts, O = sum of the
+// parts' O e^(m_p - m) / sum of l_p e^(m_p - m), parts in CTA order
+// (deterministic).  A unit's parts sit in slot 2c (its CTA c started inside
+// the unit) or 2c + 1 (CTA c started before it).  One CTA per 8 rows of a
+// unit: thread 0 finds the covering CTAs, then each warp merges one row with
+// all of its loads issued before the arithmetic.
+constexpr int kMaxParts = 8;
+
 __global__ void __launch_bounds__(256)
-    attention_combine_kernel(const float* __restrict__ part_o,
-                             const float2* __restrict__ part_ml, float* __restrict__ out,
-                             size_t rows, int d, int splits, int log2_domain) {
-  const size_t row = (blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+    attention_combine_ranges_kernel(const float* __restrict__ part_o,
+                                    const float2* __restrict__ part_ml, float* __restrict__ out,
+                                    int heads_total, int seq, int d, int causal, int ctas) {
+  __shared__ int s_parts;
+  __shared__ long long s_slot[kMaxParts];
+  const int q_blocks = (seq + kBM - 1) / kBM;
+  const long long u = blockIdx.x / (kBM / 8);
+  auto group_tiles = [&](int g) {
+    const int qb_g = q_blocks - 1 - g;
+    const int last = min(qb_g * kBM + kBM, seq) - 1;
+    return static_cast<long long>(((causal ? last + 1 : seq) + kBN - 1) / kBN);
+  };
+  if (threadIdx.x == 0) {
+    long long total = 0, start = 0;
+    const int group_u = static_cast<int>(u / heads_total);
+    for (int g = 0; g < q_blocks; ++g) {
+      const long long t = group_tiles(g);
+      if (g == group_u) start = total + (u - static_cast<long long>(g) * heads_total) * t;
+      total += t * heads_total;
+    }
+    const long long end = start + group_tiles(group_u);
+    // CTAs whose ranges [c total / ctas, (c + 1) total / ctas) meet [start, end).
+    long long c_lo = max(0LL, start * ctas / total - 1);
+    while ((c_lo + 1) * total / ctas <= start) ++c_lo;
+    int parts = 0;
+    for (long long c = c_lo; c < ctas && c * total / ctas < end && parts < kMaxParts; ++c)
+      s_slot[parts++] = 2 * c + ((c * total / ctas >= start) ? 0 : 1);
+    s_parts = parts;
+  }
+  __syncthreads();
+  const int parts = s_parts;
+  if (parts <= 1) return;  // one CTA covered the unit whole and wrote it
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = static_cast<int>(u % heads_total);
+  const int r = static_cast<int>(blockIdx.x % (kBM / 8)) * 8 + warp;
+  const int row = (q_blocks - 1 - static_cast<int>(u / heads_total)) * kBM + r;
+  if (row >= seq) return;
+  float2 ml[kMaxParts];
+  float ov[kMaxParts][4];
+#pragma unroll
+  for (int p = 0; p < kMaxParts; ++p) {
+    const bool in = p < parts;
+    ml[p] = in ? part_ml[s_slot[p] * kBM + r] : make_float2(-INFINITY, 0.0f);
+    const float* o = part_o + ((in ? s_slot[p] : 0) * kBM + r) * d;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int col = lane + 32 * i;
+      ov[p][i] = (in && col < d) ? o[col] : 0.0f;
+    }
+  }
   float m = -INFINITY;
-  for (int s = 0; s < splits; ++s) m = fmaxf(m, part_ml[static_cast<size_t>(s) * rows + row].x);
+#pragma unroll
+  for (int p = 0; p < kMaxParts; ++p) m = fmaxf(m, ml[p].x);
   float l = 0.0f;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < splits; ++s) {
-    const float2 ml = part_ml[static_cast<size_t>(s) * rows + row];
-    if (ml.x == -INFINITY) continue;  // empty chunk
-    const float w = log2_domain ? exp2f(ml.x - m) : expf(ml.x - m);
-    l += ml.y * w;
-    const float* o = part_o + (static_cast<size_t>(s) * rows + row) * d;
-    for (int c = lane, i = 0; c < d; c += 32, ++i) acc[i] += o[c] * w;
+#pragma unroll
+  for (int p = 0; p < kMaxParts; ++p) {
+    if (ml[p].x == -INFINITY) continue;
+    const float w = expf(ml[p].x - m);
+    l += ml[p].y * w;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] += ov[p][i] * w;
   }
   const float inv = 1.0f / l;
-  float* orow = out + row * d;
-  for (int c = lane, i = 0; c < d; c += 32, ++i) orow[c] = acc[i] * inv;
+  float* orow = out + (static_cast<size_t>(bh) * seq + row) * d;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int col = lane + 32 * i;
+    if (col < d) orow[col] = acc[i] * inv;
+  }
 }
 
 namespace {
@@ -304,35 +419,44 @@ cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, flo
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const long long units = static_cast<long long>(heads_total) * ((seq + kBM - 1) / kBM);
-  // Split the KV range across CTAs when the grid would leave SMs idle (and
-  // to spread the long bottom rows of causal grids): about two CTAs per SM,
-  // at least two KV tiles per chunk.
-  const int kv_tiles = (seq + kBN - 1) / kBN;
-  int splits = 1;
-  if (units < sm_count()) {
-    splits = static_cast<int>((2LL * sm_count() + units - 1) / units);
-    splits = max(1, min(splits, kv_tiles / 2));
-  }
-  const long long ctas = units * splits;
-  if (ctas > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
   const float scale = 1.0f / sqrtf(static_cast<float>(hd));
-  if (splits == 1) {
-    attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
-        q, k, v, out, heads_total, seq, hd, causal ? 1 : 0, scale, 1, nullptr, nullptr);
+  // A full grid (at least one unit per SM, and at least two KV tiles to
+  // share out): one CTA per unit.
+  const int kv_tiles = (seq + kBN - 1) / kBN;
+  if (units >= sm_count() || kv_tiles < 4) {
+    attention_f32_tiled_kernel<D><<<static_cast<unsigned>(units), kThreads, smem, stream>>>(
+        q, k, v, out, heads_total, seq, hd, causal ? 1 : 0, scale, 0, nullptr, nullptr);
     return cudaGetLastError();
   }
-  const size_t rows = static_cast<size_t>(heads_total) * seq;
+  // Grids that would leave SMs idle: the balanced schedule, one CTA per SM
+  // over equal ranges of all KV tiles (no partial last wave, and the long
+  // bottom rows of causal grids spread over several CTAs), the units split
+  // between CTAs merged afterwards.
+  // At most kMaxParts CTAs may share one unit: with R = total / grid tiles
+  // per CTA, a unit of T tiles meets at most T / R + 2 ranges.
+  long long total_tiles = 0, max_tiles = 1;
+  for (int qb = 0; qb < (seq + kBM - 1) / kBM; ++qb) {
+    const int last = std::min(qb * kBM + kBM, seq) - 1;
+    const long long t = ((causal ? last + 1 : seq) + kBN - 1) / kBN;
+    total_tiles += t * heads_total;
+    max_tiles = std::max(max_tiles, t);
+  }
+  const int grid = static_cast<int>(std::max<long long>(
+      1, std::min<long long>({static_cast<long long>(sm_count()), total_tiles,
+                              (kMaxParts - 2) * total_tiles / max_tiles})));
+  const size_t slots = 2 * static_cast<size_t>(grid);
   void* ws = nullptr;
-  e = cudaMallocAsync(&ws, rows * splits * (hd * sizeof(float) + sizeof(float2)), stream);
+  e = cudaMallocAsync(&ws, slots * kBM * (hd * sizeof(float) + sizeof(float2)), stream);
   if (e != cudaSuccess) return e;
   float* part_o = static_cast<float*>(ws);
-  float2* part_ml = reinterpret_cast<float2*>(part_o + rows * splits * hd);
-  attention_f32_tiled_kernel<D><<<static_cast<unsigned>(ctas), kThreads, smem, stream>>>(
-      q, k, v, out, heads_total, seq, hd, causal ? 1 : 0, scale, splits, part_o, part_ml);
+  float2* part_ml = reinterpret_cast<float2*>(part_o + slots * kBM * hd);
+  attention_f32_tiled_kernel<D><<<static_cast<unsigned>(grid), kThreads, smem, stream>>>(
+      q, k, v, out, heads_total, seq, hd, causal ? 1 : 0, scale, 1, part_o, part_ml);
   e = cudaGetLastError();
   if (e == cudaSuccess) {
-    attention_combine_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
-        part_o, part_ml, out, rows, hd, splits, 0);
+    attention_combine_ranges_kernel<<<static_cast<unsigned>(units * (kBM / 8)), 256, 0, stream>>>(
+        part_o, part_ml, out, heads_total, seq, hd, causal ? 1 : 0, grid);
     e = cudaGetLastError();
   }
   const cudaError_t f = cudaFreeAsync(ws, stream);

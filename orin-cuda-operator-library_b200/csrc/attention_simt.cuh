@@ -30,12 +30,4 @@ cudaError_t attention_f32_tiled(const float* q, const float* k, const float* v, 
                                 int batch, int heads, int seq, int head_dim, bool causal,
                                 cudaStream_t stream);
 
-// Merges split-KV partial attention results (per row: unnormalised O_s with
-// its (m_s, l_s)) in split order; log2_domain selects 2^x weights (tensor-
-// core kernels) instead of e^x.  One warp per row, D <= 128.
-__global__ void attention_combine_kernel(const float* __restrict__ part_o,
-                                         const float2* __restrict__ part_ml,
-                                         float* __restrict__ out, size_t rows, int d,
-                                         int splits, int log2_domain);
-
 }  // namespace opl
