@@ -176,6 +176,19 @@ def test_attention_f32(cuda, stream, b, h, s, d, causal, qk):
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("b,h,s,d,causal,qk", ATT_CASES[11:] + [
+    (1, 1, 4096, 64, False, None), (1, 1, 3001, 128, True, None)])
+def test_attention_f32_balanced_ranges(cuda, stream, b, h, s, d, causal, qk):
+    """Grids of fewer (head, query block) units than SMs run the balanced
+    schedule: every CTA takes an equal range of all KV tiles, so one unit can
+    be shared by up to 8 CTAs whose parts are merged afterwards (long rows,
+    few heads, ragged S, padded head_dim)."""
+    q, k, v = att_inputs((b, h, s, d), qk, s * 3 + d, np.float32)
+    got = run_attention(cuda, stream, q, k, v, causal)
+    want = orc.attention(q, k, v, causal)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
 def test_attention_f32_baseline_shape_all_heads(cuda, stream):
     """BASELINE FP32 attention B1 H12 S1024 D128: every head, both masks,
     against the oracle's full loop (reference gate atol = rtol = 1e-4)."""
