@@ -193,21 +193,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
 
-    // S = Q K^T for rows 8tr.., keys 4tc..: s2[i][0..1] hold key pairs.
-    uint64_t s2[8][2];
+    // S = Q K^T for rows 8tr.., keys 4tc..: s2[r][j] holds rows (2r, 2r + 1)
+    // of key j, so the Q operand pairs come straight from the 128-bit loads
+    // and only the four K values are duplicated.
+    uint64_t s2[4][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) s2[i][0] = s2[i][1] = 0;
-#pragma unroll 4
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s2[r][j] = 0;
+#pragma unroll 8
     for (int d = 0; d < D; ++d) {
-      const float4 qa = *reinterpret_cast<const float4*>(&qt[d * Cfg::kQPitch + tr * 8]);
-      const float4 qb4 = *reinterpret_cast<const float4*>(&qt[d * Cfg::kQPitch + tr * 8 + 4]);
-      const ulonglong2 kk = *reinterpret_cast<const ulonglong2*>(&kt[d * Cfg::kKPitch + tc * 4]);
-      const float qv[8] = {qa.x, qa.y, qa.z, qa.w, qb4.x, qb4.y, qb4.z, qb4.w};
+      const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(&qt[d * Cfg::kQPitch + tr * 8]);
+      const ulonglong2 qb = *reinterpret_cast<const ulonglong2*>(&qt[d * Cfg::kQPitch + tr * 8 + 4]);
+      const float4 kk = *reinterpret_cast<const float4*>(&kt[d * Cfg::kKPitch + tc * 4]);
+      const uint64_t qp[4] = {qa.x, qa.y, qb.x, qb.y};
+      const float kv[4] = {kk.x, kk.y, kk.z, kk.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint64_t a = dup2f(qv[i]);
-        fma2f(s2[i][0], a, kk.x);
-        fma2f(s2[i][1], a, kk.y);
+      for (int j = 0; j < 4; ++j) {
+        const uint64_t b = dup2f(kv[j]);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) fma2f(s2[r][j], qp[r], b);
       }
     }
 
@@ -216,8 +221,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 8; ++i) {
       const int row = q0 + tr * 8 + i;
       float s[4];
-      unpack2f(s2[i][0], s[0], s[1]);
-      unpack2f(s2[i][1], s[2], s[3]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float lo, hi;
+        unpack2f(s2[i >> 1][j], lo, hi);
+        s[j] = (i & 1) ? hi : lo;
+      }
       float tile_max = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -255,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // O += P V over this tile's keys.
     const int key_count = min(kBN, seq - k0);
-#pragma unroll 2
+#pragma unroll 4
     for (int j = 0; j < key_count; ++j) {
       const float4 pa = *reinterpret_cast<const float4*>(&pt[j * Cfg::kPPitch + tr * 8]);
       const float4 pb = *reinterpret_cast<const float4*>(&pt[j * Cfg::kPPitch + tr * 8 + 4]);
