@@ -409,6 +409,7 @@ struct PadJob {
   int prow, pcol;
 };
 
+// Fallback for rows too long for pad_rows_bulk_kernel's shared-memory ring.
 // Both operands' padded copies in ONE launch, one CTA per destination row
 // (job 0's rows first, then job 1's).  Within a warp, lane l writes group
 // g0 + l (8 halves = 16 bytes) of the row: it loads the one aligned 16-byte
@@ -527,6 +528,194 @@ __global__ void __launch_bounds__(kPadThreads)
 #pragma unroll
       for (int w = 0; w < kPadThreads / 32; ++w) v += part[w][threadIdx.x];
       c[static_cast<size_t>(r) * ldc + threadIdx.x] = v;
+    }
+  }
+}
+
+// The padding pass with the source rows fetched by the copy engine: a
+// persistent grid (kBulkCtasPerSm CTAs per SM) in which each CTA streams its
+// rows (item w, w + P, ...) into
+// a kBulkStages-deep shared-memory ring with one cp.async.bulk per row (the
+// 16-byte-aligned words spanning the row: every word holds bytes of the row,
+// so nothing outside the caller's matrix is read), completion on an mbarrier
+// per stage; its threads then shift each staged row into place and write
+// the padded row with coalesced 16-byte stores (and, for A's rows, the
+// narrow remainder's dot: per-thread sums in group order, warp xor trees,
+// then the warps in order, so results repeat bit for bit).  Up to
+// kBulkStages rows per CTA are in flight without holding registers.  The
+// dot's warp sums go to a ring of kDotRing rows and lanes of the last warp
+// finish each row after the barrier that releases its stage, so the dot
+// adds no barrier of its own; the CTAs zero the GEMM's split tail tiles
+// while their first rows arrive.  Waits are bounded; a CTA that gives up
+// trips the watchdog, waits (bounded) for its copies in flight and returns.
+// 4095 x 4097 x 4093: 30 us against 38 us for pad_rows_kernel (one CTA per
+// row, zeroing CTAs of their own), the copy alone ~23 us.
+constexpr int kBulkStages = 4;
+constexpr int kBulkCtasPerSm = 4;
+
+__device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint32_t bytes,
+                                             uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kPadThreads)
+    pad_rows_bulk_kernel(PadJob j0, PadJob j1, const __half* __restrict__ bt, int n_tail,
+                         float* __restrict__ c, int ldc, TailZeroJob zero, int stage_bytes,
+                         int* watchdog) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ uint64_t full[kBulkStages];
+  // Dot partials of the last kDotRing rows: part[row % kDotRing][warp][t].
+  constexpr int kDotRing = 8;
+  __shared__ float part[kDotRing][kPadThreads / 32][kPadDotMaxTail];
+  __shared__ int abort_flag;
+  const int w = static_cast<int>(blockIdx.x);
+  const int workers = static_cast<int>(gridDim.x);
+  const int rows_total = j0.prow + j1.prow;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBulkStages; ++s) tc::mbar_init(&full[s], 1);
+    abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  const uint32_t ring_base = tc::smem_u32(ring);
+  // Source range of item i's row: the aligned words holding it (bytes == 0:
+  // a zero row past the source, nothing to load).
+  auto source = [&](int item, const __half*& src, uint32_t& bytes, int& lead) {
+    const bool second = item >= j0.prow;
+    const PadJob& job = second ? j1 : j0;
+    const int r = second ? item - j0.prow : item;
+    bytes = 0;
+    lead = 0;
+    src = nullptr;
+    if (r >= job.rows) return;
+    const uintptr_t start = reinterpret_cast<uintptr_t>(job.src + static_cast<size_t>(r) * job.cols);
+    const uintptr_t end = start + static_cast<uintptr_t>(job.cols) * 2;
+    const uintptr_t a0 = start & ~uintptr_t(15), a1 = (end + 15) & ~uintptr_t(15);
+    src = reinterpret_cast<const __half*>(a0);
+    bytes = static_cast<uint32_t>(a1 - a0);
+    lead = static_cast<int>((start & 15u) >> 1);
+  };
+  uint32_t pending = 0;  // thread 0: stages with a copy issued and not consumed
+  auto issue = [&](int i) {  // thread 0
+    const int item = w + i * workers;
+    if (item >= rows_total) return;
+    const __half* src;
+    uint32_t bytes;
+    int lead;
+    source(item, src, bytes, lead);
+    if (bytes == 0) return;
+    const int st = i % kBulkStages;
+    pending |= 1u << st;
+    tc::mbar_expect_tx(&full[st], bytes);
+    bulk_load_1d(ring_base + st * stage_bytes, src, bytes, tc::smem_u32(&full[st]));
+  };
+  if (threadIdx.x == 0)
+    for (int i = 0; i < kBulkStages; ++i) issue(i);
+  // The GEMM's split tail tiles are zeroed while the first rows arrive.
+  for (int z = w; z < 16 * zero.tail; z += workers)
+    zero_tail_slice<kPairBM>(zero.c, zero.m, zero.n, zero.k, zero.ldc, zero.pairs,
+                             zero.group_m, z >> 4, z & 15);
+  // Lanes 0 .. n_tail - 1 of the last warp finish each row's dot.
+  const int fin = static_cast<int>(threadIdx.x) - (kPadThreads - 32);
+  uint32_t phases = 0;  // parity per stage (loaded rows only)
+  bool ok = true;
+  for (int i = 0;; ++i) {
+    const int item = w + i * workers;
+    if (item >= rows_total) break;
+    const bool second = item >= j0.prow;
+    const PadJob& job = second ? j1 : j0;
+    const int r = second ? item - j0.prow : item;
+    const int st = i % kBulkStages;
+    const __half* src;
+    uint32_t bytes;
+    int lead;
+    source(item, src, bytes, lead);
+    if (bytes > 0) {
+      const bool got = tc::mbar_wait(&full[st], (phases >> st) & 1u, &abort_flag, watchdog,
+                                     tc::kWatchdogGemm);
+      if (!__syncthreads_and(got)) {
+        ok = false;
+        break;
+      }
+      phases ^= 1u << st;
+      pending &= ~(1u << st);
+    }
+    const uint4* staged = reinterpret_cast<const uint4*>(ring + st * stage_bytes);
+    uint4* drow = reinterpret_cast<uint4*>(job.dst + static_cast<size_t>(r) * job.pcol);
+    const int groups = job.pcol / 8;
+    const bool dot = second && n_tail > 0;
+    float acc[kPadDotMaxTail];
+#pragma unroll
+    for (int t = 0; t < kPadDotMaxTail; ++t) acc[t] = 0.0f;
+    for (int g = threadIdx.x; g < groups; g += kPadThreads) {
+      uint4 out = make_uint4(0, 0, 0, 0);
+      const int valid = bytes > 0 ? job.cols - g * 8 : 0;  // halves of this group in the row
+      if (valid > 0) {
+        const uint4 lo = staged[g], hi = staged[g + 1];
+        const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+        out = halves_at(wv, lead);
+        if (valid < 8) {
+          uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            if (2 * q >= valid) ow[q] = 0;
+            else if (2 * q + 1 >= valid) ow[q] &= 0xffffu;
+          }
+        }
+      }
+      drow[g] = out;
+      if (dot) {
+        const __half2* a2 = reinterpret_cast<const __half2*>(&out);
+#pragma unroll
+        for (int t = 0; t < kPadDotMaxTail; ++t) {
+          if (t < n_tail) {
+            const uint4 bv =
+                __ldg(reinterpret_cast<const uint4*>(bt + static_cast<size_t>(t) * job.pcol) + g);
+            const __half2* b2 = reinterpret_cast<const __half2*>(&bv);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 af = __half22float2(a2[q]);
+              const float2 bf = __half22float2(b2[q]);
+              acc[t] = fmaf(af.x, bf.x, acc[t]);
+              acc[t] = fmaf(af.y, bf.y, acc[t]);
+            }
+          }
+        }
+      }
+    }
+    if (dot) {  // CTA-uniform
+#pragma unroll
+      for (int t = 0; t < kPadDotMaxTail; ++t) {
+        if (t < n_tail) {
+          const float v = warp_sum(acc[t]);
+          if (lane == 0) part[i % kDotRing][warp][t] = v;
+        }
+      }
+    }
+    __syncthreads();  // the stage is consumed (and the dot partials are in)
+    if (threadIdx.x == 0) issue(i + kBulkStages);
+    // Row i's slot is written again only at row i + kDotRing, after
+    // kDotRing - 1 more barriers, so no barrier guards this read.
+    if (dot && fin >= 0 && fin < n_tail) {
+      float v = 0.0f;
+#pragma unroll
+      for (int q = 0; q < kPadThreads / 32; ++q) v += part[i % kDotRing][q][fin];
+      c[static_cast<size_t>(r) * ldc + fin] = v;
+    }
+  }
+  if (!ok && threadIdx.x == 0) {
+    // Copies this CTA issued and did not consume: wait for them (bounded)
+    // before the CTA's shared memory is released.
+    for (int s = 0; s < kBulkStages; ++s) {
+      if (!((pending >> s) & 1u)) continue;
+      const uint32_t a = tc::smem_u32(&full[s]);
+      const uint64_t t0 = globaltimer_ns();
+      while (!tc::mbar_try_wait(a, (phases >> s) & 1u) && globaltimer_ns() - t0 < tc::kMaxWaitNs) {
+      }
     }
   }
 }
@@ -903,11 +1092,31 @@ cudaError_t gemm_f16_tc(const __half* a, const __half* b, float* c, int m, int n
     // (a block count beyond grid.x's limit fails to launch; the error is returned)
     const long long blocks =
         static_cast<long long>(jobs[0].prow) + jobs[1].prow + 16LL * zero.tail;
-    pad_rows_kernel<<<static_cast<unsigned>(blocks), kPadThreads, 0, stream>>>(
-        jobs[0], jobs[1], bt, tail_in_pad ? n_tail : 0, c + n_main, n, zero);
+    // Ring stage: the widest staged row plus the one word the shift reads past
+    // the last group.
+    int words = 0;
+    for (int j = 0; j < 2; ++j)
+      if (jobs[j].prow > 0)
+        words = std::max({words, jobs[j].pcol / 8, (jobs[j].cols + 7 + 7) / 8});
+    const int stage_bytes = ((words + 1) * 16 + 127) & ~127;
+    const int ring = kBulkStages * stage_bytes;
+    const int per_sm = std::min(kBulkCtasPerSm, (200 * 1024) / ring);
+    if (per_sm >= 1) {
+      e = cudaFuncSetAttribute(pad_rows_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               ring);
+      if (e == cudaSuccess) {
+        const int bulk_blocks = per_sm * sm_count();
+        pad_rows_bulk_kernel<<<bulk_blocks, kPadThreads, ring, stream>>>(
+            jobs[0], jobs[1], bt, tail_in_pad ? n_tail : 0, c + n_main, n, zero, stage_bytes,
+            watchdog_word());
+      }
+    } else {
+      pad_rows_kernel<<<static_cast<unsigned>(blocks), kPadThreads, 0, stream>>>(
+          jobs[0], jobs[1], bt, tail_in_pad ? n_tail : 0, c + n_main, n, zero);
+    }
     tail_zeroed = true;
   }
-  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaGetLastError();
   const int lda = a_ok ? k : kp;
   const int ldb = b_ok ? n : ldb_copy;
   if (e == cudaSuccess)

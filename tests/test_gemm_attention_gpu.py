@@ -52,7 +52,9 @@ GEMM_F16 = [(128, 128, 32), (16, 128, 32), (32, 32, 32), (37, 65, 71),  # ref te
             # ragged K with a remainder of <= 8 columns: computed in A's padding pass
             (300, 262, 77), (200, 520, 45), (1000, 1033, 999),
             # larger padded products (both operands / a 1-column remainder)
-            (2048, 2304, 2050), (2304, 2561, 1999)]
+            (2048, 2304, 2050), (2304, 2561, 1999),
+            # padded rows too long for the bulk-copy ring: per-row fallback
+            (256, 264, 26001), (300, 26001, 64)]
 
 
 @pytest.mark.parametrize("m,n,k", GEMM_F16)
