@@ -431,13 +431,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Raw-score maximum (scale > 0 commutes with max); eight independent
       // partial maxima / sums keep dependency chains short.
+      // pm[a] = max of s[a], s[a + 8], ...: s[0 .. 7], then 16 scores per
+      // step, then the last 8 when (kKeys - 8) is an odd multiple of 8.
       float pm[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) pm[a] = fmax3(s[a], s[8 + a], s[16 + a]);
+      for (int a = 0; a < 8; ++a) pm[a] = s[a];
 #pragma unroll
-      for (int i = 24; i < kKeys; i += 16) {
+      for (int i = 8; i + 16 <= kKeys; i += 16) {
 #pragma unroll
         for (int a = 0; a < 8; ++a) pm[a] = fmax3(pm[a], s[i + a], s[i + 8 + a]);
+      }
+      if constexpr ((kKeys - 8) % 16 == 8) {
+#pragma unroll
+        for (int a = 0; a < 8; ++a) pm[a] = fmaxf(pm[a], s[kKeys - 8 + a]);
       }
       const float mx = scale_log2 * fmax3(fmax3(pm[0], pm[1], pm[2]), fmax3(pm[3], pm[4], pm[5]),
                                           fmaxf(pm[6], pm[7]));
