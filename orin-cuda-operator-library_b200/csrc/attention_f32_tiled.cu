@@ -87,7 +87,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // it covers in part (at most its first and last segments) to partial slot
   // 2 blockIdx.x (first) or 2 blockIdx.x + 1 (last), which
   // attention_combine_ranges_kernel merges.
-  const long long units = static_cast<long long>(heads_total) * q_blocks;
   auto unit_tiles = [&](long long u) {
     const int qb_u = q_blocks - 1 - static_cast<int>(u / heads_total);
     const int last = min(qb_u * kBM + kBM, seq) - 1;

@@ -359,43 +359,6 @@ __device__ __forceinline__ uint4 halves_at(const uint32_t (&w)[8], int o) {
   return make_uint4(r[0], r[1], r[2], r[3]);
 }
 
-// Source words of a rows x cols FP16 matrix at any 2-byte-aligned base: the
-// 16-byte-aligned word holding the first element (inside the caller's
-// allocation, whose base is 256-byte aligned) and the element offset to it.
-struct HalfRows {
-  const uint4* src4;
-  size_t lead;          // halves before the first element in its word
-  size_t total_chunks;  // 16-byte words covering the matrix
-  int cols;
-  __device__ HalfRows(const __half* src, int rows, int cols_) : cols(cols_) {
-    const uintptr_t addr = reinterpret_cast<uintptr_t>(src);
-    lead = (addr & 15u) >> 1;
-    src4 = reinterpret_cast<const uint4*>(addr & ~uintptr_t(15));
-    total_chunks = (lead + static_cast<size_t>(rows) * cols + 7) / 8;
-  }
-  // Halves [8g, 8g + 8) of row r, zero past the row's end: built from the two
-  // aligned 16-byte words that cover them and a per-row byte shift, so all
-  // loads are 128-bit.
-  __device__ __forceinline__ uint4 group(int r, int g) const {
-    const size_t row_h = lead + static_cast<size_t>(r) * cols;
-    const size_t c0 = (row_h + static_cast<size_t>(g) * 8) >> 3;
-    const uint4 lo = __ldg(src4 + c0);
-    const uint4 hi = c0 + 1 < total_chunks ? __ldg(src4 + c0 + 1) : make_uint4(0, 0, 0, 0);
-    const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-    uint4 out = halves_at(w, static_cast<int>(row_h & 7));
-    const int valid = cols - g * 8;  // halves of this group inside the row
-    if (valid < 8) {
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (2 * i >= valid) ow[i] = 0;
-        else if (2 * i + 1 >= valid) ow[i] &= 0xffffu;
-      }
-    }
-    return out;
-  }
-};
-
 // Widest N remainder whose product the A-padding pass computes itself.
 constexpr int kPadDotMaxTail = 8;
 
