@@ -216,6 +216,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // Online softmax per row; the 16 lanes sharing tr hold the row's 64 keys.
+    // P goes to shared memory after the loop, rows 8tr .. 8tr + 7 of each key
+    // as two 128-bit stores.
+    float pr[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int row = q0 + tr * 8 + i;
@@ -257,7 +260,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         o2[i][c] = scaled;
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) pt[(tc * 4 + j) * Cfg::kPPitch + tr * 8 + i] = s[j];
+      for (int j = 0; j < 4; ++j) pr[i][j] = s[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float* dst = &pt[(tc * 4 + j) * Cfg::kPPitch + tr * 8];
+      *reinterpret_cast<float4*>(dst) = make_float4(pr[0][j], pr[1][j], pr[2][j], pr[3][j]);
+      *reinterpret_cast<float4*>(dst + 4) = make_float4(pr[4][j], pr[5][j], pr[6][j], pr[7][j]);
     }
     __syncthreads();
 
