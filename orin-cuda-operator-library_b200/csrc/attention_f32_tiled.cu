@@ -9,7 +9,8 @@
 //             fragment (Q stored d-major in shared memory, two 128-bit loads)
 //             and one 4-key K fragment (K stored d-major, one 128-bit load);
 //   softmax   row max / sum across the 16 lanes of a row group (xor
-//             shuffles), online rescaling of O;
+//             shuffles), online rescaling of O; scores in the log2 domain,
+//             exponentials by the MUFU ex2 instruction;
 //   PV phase  O[8 rows][D/16 columns] += P V over the 64 keys: P stored
 //             key-major (8-row fragment = two 128-bit loads), V row-major.
 // Register-tile updates use packed fma.rn.f32x2 (two independent FP32 FMAs
@@ -43,6 +44,12 @@ __device__ __forceinline__ uint64_t pack2f(float lo, float hi) {
 __device__ __forceinline__ void fma2f(uint64_t& acc, uint64_t a, uint64_t b) {
   asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
 }
+// 2^x on the MUFU unit (ex2.approx, relative error ~2^-22; 2^-inf = 0).
+__device__ __forceinline__ float exp2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void unpack2f(uint64_t v, float& lo, float& hi) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
@@ -64,7 +71,7 @@ template <int D>
 __global__ void __launch_bounds__(kThreads, 1)
     attention_f32_tiled_kernel(const float* __restrict__ q, const float* __restrict__ k,
                                const float* __restrict__ v, float* __restrict__ out,
-                               int heads_total, int seq, int hd, int causal, float scale,
+                               int heads_total, int seq, int hd, int causal, float scale_log2,
                                int balanced, float* __restrict__ part_o,
                                float2* __restrict__ part_ml) {
   using Cfg = F32Cfg<D>;
@@ -234,18 +241,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < 4; ++j) {
         const int key = k0 + tc * 4 + j;
         const bool valid = key < seq && (!causal || key <= row);
-        s[j] = valid ? s[j] * scale : -INFINITY;
+        s[j] = valid ? s[j] * scale_log2 : -INFINITY;  // log2 domain
         tile_max = fmaxf(tile_max, s[j]);
       }
 #pragma unroll
       for (int o = 8; o > 0; o >>= 1)
         tile_max = fmaxf(tile_max, __shfl_xor_sync(kFullMask, tile_max, o));
       const float m_new = fmaxf(m_run[i], tile_max);
-      const float alpha = (m_new == -INFINITY) ? 1.0f : expf(m_run[i] - m_new);
+      const float alpha = (m_new == -INFINITY) ? 1.0f : exp2_mufu(m_run[i] - m_new);
       float tile_sum = 0.0f;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        s[j] = (s[j] == -INFINITY) ? 0.0f : expf(s[j] - m_new);
+        s[j] = (s[j] == -INFINITY) ? 0.0f : exp2_mufu(s[j] - m_new);
         tile_sum += s[j];
       }
 #pragma unroll
@@ -344,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Merges the partial results of the balanced schedule: for every unit that
 // more than one CTA covered, per row, m = max over its parts, O = sum of the
-// parts' O e^(m_p - m) / sum of l_p e^(m_p - m), parts in CTA order
+// parts' O 2^(m_p - m) / sum of l_p 2^(m_p - m) (log2 domain), parts in CTA order
 // (deterministic).  A unit's parts sit in slot 2c (its CTA c started inside
 // the unit) or 2c + 1 (CTA c started before it).  One CTA per 8 rows of a
 // unit: thread 0 finds the covering CTAs, then each warp merges one row with
@@ -410,7 +417,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int p = 0; p < kMaxParts; ++p) {
     if (ml[p].x == -INFINITY) continue;
-    const float w = expf(ml[p].x - m);
+    const float w = exp2f(ml[p].x - m);  // (m, l) are in the log2 domain
     l += ml[p].y * w;
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i] += ov[p][i] * w;
@@ -437,7 +444,8 @@ cudaError_t launch_f32_tiled(const float* q, const float* k, const float* v, flo
   if (e != cudaSuccess) return e;
   const long long units = static_cast<long long>(heads_total) * ((seq + kBM - 1) / kBM);
   if (units > 0x7fffffffLL) return cudaErrorInvalidValue;
-  const float scale = 1.0f / sqrtf(static_cast<float>(hd));
+  // Scores are kept in the log2 domain: 2^(s log2(e) / sqrt(d) - m) = e^(s / sqrt(d) - m').
+  const float scale = 1.4426950408889634f / sqrtf(static_cast<float>(hd));
   // A full grid (at least one unit per SM, and at least two KV tiles to
   // share out): one CTA per unit.
   const int kv_tiles = (seq + kBN - 1) / kBN;
