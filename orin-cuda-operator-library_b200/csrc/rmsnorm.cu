@@ -10,8 +10,11 @@
 
 namespace opl {
 
+// At most 64 registers (1024 threads per SM), as the softmax kernel of the
+// same shape: 4097 x 1023 is 1,025 CTAs of 128 threads, one wave at 8 CTAs
+// per SM but 1.15 waves at the 6 that 80 registers allowed.
 template <int kGroup, int kBlock, int kItems, bool kVec>
-__global__ void __launch_bounds__(kBlock)
+__global__ void __launch_bounds__(kBlock, 1024 / kBlock)
     rmsnorm_cached_kernel(const float* __restrict__ input,
                           const float* __restrict__ weight,
                           float* __restrict__ output, int tokens, int hidden,
