@@ -20,6 +20,7 @@ constexpr int kT4Threads = 256;
 __global__ void __launch_bounds__(kT4Threads)
     transpose_vec4_kernel(const float* __restrict__ input,
                           float* __restrict__ output, int rows, int cols) {
+  pdl_begin();
   __shared__ float tile[kT4][kT4 + 1];
   const int tile_col = blockIdx.x * kT4;  // input column origin
   const int c4 = threadIdx.x & 15;        // float4 column inside the tile
@@ -121,8 +122,8 @@ extern "C" int opl_transpose_f32(const float* input, float* output, int rows,
     return cudaErrorInvalidValue;
   if (rows % 4 == 0 && cols % 4 == 0 && aligned16(input) && aligned16(output)) {
     const dim3 grid = tile_grid(rows, cols, kT4);
-    transpose_vec4_kernel<<<grid, kT4Threads, 0, stream>>>(input, output, rows,
-                                                            cols);
+    return launch_pdl(transpose_vec4_kernel, grid, dim3(kT4Threads), stream, input, output,
+                      rows, cols);
   } else {
     const dim3 grid = tile_grid(rows, cols, kT1);
     return launch_pdl(transpose_scalar_kernel, grid, dim3(kT1, kT1Rows), stream, input,
