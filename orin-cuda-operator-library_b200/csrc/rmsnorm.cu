@@ -23,13 +23,22 @@ __global__ void __launch_bounds__(kBlock, 1024 / kBlock)
   constexpr int kWidth = RowElems<kVec>::kWidth;
   constexpr int kRowsPerBlock = kBlock / kGroup;
   __shared__ float scratch[kBlock / 32];
+  // Scalar warp-per-row shapes: w (at most 32 kItems floats) staged in shared
+  // memory once per CTA, after the row's own loads are issued.
+  constexpr bool kStageW = !kVec && kGroup == 32;
+  __shared__ float w_s[kStageW ? kItems * 32 : 1];
   const int t = threadIdx.x % kGroup;
   const int row = blockIdx.x * kRowsPerBlock + threadIdx.x / kGroup;
-  if (kGroup == 32 && row >= tokens) return;
-  const std::size_t offset = static_cast<std::size_t>(row) * hidden;
+  const bool active = !(kGroup == 32 && row >= tokens);
+  const std::size_t offset = static_cast<std::size_t>(active ? row : 0) * hidden;
 
   float v[kItems * kWidth];
-  load_row<kGroup, kItems, kVec>(input + offset, hidden, t, 0.0f, v);
+  if (active) load_row<kGroup, kItems, kVec>(input + offset, hidden, t, 0.0f, v);
+  if constexpr (kStageW) {
+    for (int c = threadIdx.x; c < hidden; c += kBlock) w_s[c] = __ldg(weight + c);
+    __syncthreads();
+  }
+  if (!active) return;
   float sq = 0.0f;
 #pragma unroll
   for (int i = 0; i < kItems * kWidth; ++i) sq = fmaf(v[i], v[i], sq);
@@ -53,7 +62,11 @@ __global__ void __launch_bounds__(kBlock, 1024 / kBlock)
 #pragma unroll
     for (int j = 0; j < kItems; ++j) {
       const int col = t + j * kGroup;
-      if (col < hidden) v[j] = v[j] * inverse_rms * __ldg(weight + col);
+      if constexpr (kStageW) {
+        if (col < hidden) v[j] = v[j] * inverse_rms * w_s[col];
+      } else {
+        if (col < hidden) v[j] = v[j] * inverse_rms * __ldg(weight + col);
+      }
     }
   }
   store_row<kGroup, kItems, kVec>(output + offset, hidden, t, v);
