@@ -189,14 +189,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       kt[(4 * c4 + 2) * Cfg::kKPitch + key] = x.z;
       kt[(4 * c4 + 3) * Cfg::kKPitch + key] = x.w;
     }
+    // V by 16-byte cp.async: it lands while the S phase and the softmax run
+    // (waited for before the PV phase); out-of-range pieces are zeroed.
     for (int idx = tid; idx < kBN * (D / 4); idx += kThreads) {
       const int key = idx / (D / 4);
       const int c4 = idx % (D / 4);
-      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (k0 + key < seq && 4 * c4 < hd)
-        x = __ldg(reinterpret_cast<const float4*>(v + base + static_cast<size_t>(k0 + key) * hd) + c4);
-      *reinterpret_cast<float4*>(&vs[key * Cfg::kVPitch + 4 * c4]) = x;
+      float* dst = &vs[key * Cfg::kVPitch + 4 * c4];
+      if (k0 + key < seq && 4 * c4 < hd) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                     "l"(v + base + static_cast<size_t>(k0 + key) * hd + 4 * c4)
+                     : "memory");
+      } else {
+        *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
     __syncthreads();
 
     // S = Q K^T for rows 8tr.., keys 4tc..: s2[r][j] holds rows (2r, 2r + 1)
@@ -275,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       *reinterpret_cast<float4*>(dst) = make_float4(pr[0][j], pr[1][j], pr[2][j], pr[3][j]);
       *reinterpret_cast<float4*>(dst + 4) = make_float4(pr[4][j], pr[5][j], pr[6][j], pr[7][j]);
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");  // this thread's V pieces landed
     __syncthreads();
 
     // O += P V over this tile's keys.
