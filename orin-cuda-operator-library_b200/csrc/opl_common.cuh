@@ -51,6 +51,37 @@ __device__ __forceinline__ float ld_stream(const float* p) {
   return r;
 }
 
+// Read-only loads as volatile asm.  In kernels launched with programmatic
+// dependent launch, loads must stay after griddepcontrol.wait: an __ldg, or a
+// plain load through a const __restrict__ pointer, lets the compiler assume
+// the data never changes during the kernel and move the load ahead of the
+// wait, where it can read what the previous kernel has not written yet.
+__device__ __forceinline__ float ld_ro(const float* p) {
+  float r;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(r) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ float4 ld_ro(const float4* p) {
+  float4 r;
+  asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint4 ld_ro(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+// Coherent load of a value another grid wrote (FP64 partial sums).
+__device__ __forceinline__ double ld_coherent(const double* p) {
+  double r;
+  asm volatile("ld.global.f64 %0, [%1];" : "=d"(r) : "l"(p));
+  return r;
+}
+
 // Streaming stores: outputs are written once and not re-read by the kernel.
 __device__ __forceinline__ void st_stream(float4* p, float4 v) { __stcs(p, v); }
 __device__ __forceinline__ void st_stream(float* p, float v) { __stcs(p, v); }

@@ -38,7 +38,7 @@ __device__ __forceinline__ double sum_partials_strided(const double* __restrict_
 #pragma unroll
   for (int u = 0; u < kPer; ++u) {
     const int i = static_cast<int>(threadIdx.x) + u * kReduceThreads;
-    vals[u] = i < count ? partials[i] : 0.0;
+    vals[u] = i < count ? ld_coherent(partials + i) : 0.0;  // after griddepcontrol.wait
   }
   double v = 0.0;
 #pragma unroll

@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(kBlock, 1024 / kBlock)
   float v[kItems * kWidth];
   if (active) load_row<kGroup, kItems, kVec>(input + offset, hidden, t, 0.0f, v);
   if constexpr (kStageW) {
-    for (int c = threadIdx.x; c < hidden; c += kBlock) w_s[c] = __ldg(weight + c);
+    for (int c = threadIdx.x; c < hidden; c += kBlock) w_s[c] = ld_ro(weight + c);
     __syncthreads();
   }
   if (!active) return;
@@ -51,7 +51,7 @@ __global__ void __launch_bounds__(kBlock, 1024 / kBlock)
     for (int j = 0; j < kItems; ++j) {
       const int idx = t + j * kGroup;
       if (idx < (hidden >> 2)) {
-        const float4 w = __ldg(w4 + idx);
+        const float4 w = ld_ro(w4 + idx);
         v[4 * j + 0] = v[4 * j + 0] * inverse_rms * w.x;
         v[4 * j + 1] = v[4 * j + 1] * inverse_rms * w.y;
         v[4 * j + 2] = v[4 * j + 2] * inverse_rms * w.z;
@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kBlock, 1024 / kBlock)
       if constexpr (kStageW) {
         if (col < hidden) v[j] = v[j] * inverse_rms * w_s[col];
       } else {
-        if (col < hidden) v[j] = v[j] * inverse_rms * __ldg(weight + col);
+        if (col < hidden) v[j] = v[j] * inverse_rms * ld_ro(weight + col);
       }
     }
   }
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kRmsSplitThreads, 16)
     const int idx = t + j * kRmsSplitThreads;
     if (idx < vectors) {
       const float4 u = j < 4 ? v[j] : half_row[t + (j - 4) * kRmsSplitThreads];
-      const float4 w = __ldg(w4 + idx);
+      const float4 w = ld_ro(w4 + idx);
       st_stream(y4 + idx, make_float4(u.x * inverse_rms * w.x, u.y * inverse_rms * w.y,
                                       u.z * inverse_rms * w.z, u.w * inverse_rms * w.w));
     }
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(kRmsLongThreads)
   const float inverse_rms = rsqrtf(sq / static_cast<float>(hidden) + epsilon);
   float* out = output + offset;
   for (int c = threadIdx.x; c < hidden; c += kRmsLongThreads)
-    st_stream(out + c, row[c] * inverse_rms * __ldg(weight + c));
+    st_stream(out + c, row[c] * inverse_rms * ld_ro(weight + c));
 }
 
 }  // namespace opl

@@ -49,7 +49,7 @@ __device__ __forceinline__ void load16(const T* __restrict__ row, int cols, int 
     for (int j = 0; j < kItems; ++j) {
       const int idx = t + j * kGroup;
       if (idx < vectors) {
-        uint4 raw = __ldg(row8 + idx);
+        uint4 raw = ld_ro(row8 + idx);
         const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[8 * j + i] = Io16<T>::load(e[i]);
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(kBlock)
     if constexpr (kVec) {
       const int idx = t + j * kGroup;
       if (idx < (hidden >> 3)) {
-        uint4 raw = __ldg(reinterpret_cast<const uint4*>(weight) + idx);
+        uint4 raw = ld_ro(reinterpret_cast<const uint4*>(weight) + idx);
         const T* e = reinterpret_cast<const T*>(&raw);
 #pragma unroll
         for (int i = 0; i < 8; ++i) w[i] = Io16<T>::load(e[i]);

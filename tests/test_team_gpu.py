@@ -49,6 +49,19 @@ def _rank_main(rank, world, port, q):
             team.reduce_sum_into(chunk, out)
             torch.cuda.synchronize()
             results.append((out.item(), orc.reduce_sum(x)))
+        # back-to-back calls alternating two inputs of the same size: a
+        # finalize that read its partials before the partial kernel wrote
+        # them would pick up the other input's (same workspace memory)
+        xa = np.random.default_rng(11).uniform(-1, 1, 16_777_216).astype(np.float32)
+        xb = np.random.default_rng(12).uniform(-1, 1, 16_777_216).astype(np.float32)
+        lo, hi = bench.shard_range(xa.size, world, rank)
+        ca, cb = (torch.from_numpy(v[lo:hi].copy()).cuda() for v in (xa, xb))
+        outs = torch.empty(6, device="cuda")
+        for k in range(6):
+            team.reduce_sum_into(ca if k % 2 == 0 else cb, outs[k])
+        torch.cuda.synchronize()
+        for k in range(6):
+            results.append((outs[k].item(), orc.reduce_sum(xa if k % 2 == 0 else xb)))
         # one captured call replayed three times
         x = np.random.default_rng(7).uniform(-1, 1, 2_000_000).astype(np.float32)
         lo, hi = bench.shard_range(x.size, world, rank)
