@@ -78,7 +78,7 @@ __device__ __forceinline__ uint4 ld_ro(const uint4* p) {
 // Coherent load of a value another grid wrote (FP64 partial sums).
 __device__ __forceinline__ double ld_coherent(const double* p) {
   double r;
-  asm volatile("ld.global.f64 %0, [%1];" : "=d"(r) : "l"(p));
+  asm volatile("ld.global.cg.f64 %0, [%1];" : "=d"(r) : "l"(p));  // L2, never a stale L1 line
   return r;
 }
 

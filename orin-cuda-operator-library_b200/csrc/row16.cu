@@ -20,13 +20,26 @@ struct Io16;
 template <>
 struct Io16<__half> {
   static __device__ __forceinline__ float load(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_bits(unsigned short b) { return __ushort_as_half(b); }
   static __device__ __forceinline__ __half store(float f) { return __float2half_rn(f); }
 };
 template <>
 struct Io16<__nv_bfloat16> {
   static __device__ __forceinline__ float load(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_bits(unsigned short b) {
+    return __ushort_as_bfloat16(b);
+  }
   static __device__ __forceinline__ __nv_bfloat16 store(float f) { return __float2bfloat16_rn(f); }
 };
+
+// One 16-bit element by a volatile-asm load (kept after griddepcontrol.wait;
+// see ld_ro), as FP32.
+template <typename T>
+__device__ __forceinline__ float ld_ro16(const T* p) {
+  unsigned short b;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(b) : "l"(p));
+  return Io16<T>::load(Io16<T>::from_bits(b));
+}
 
 // e^x as 2^(x log2 e) on the MUFU ex2 unit (ex2.approx.f32, relative error
 // about 2^-22; subnormal results kept).  With x = v - m formed first, the
@@ -62,7 +75,7 @@ __device__ __forceinline__ void load16(const T* __restrict__ row, int cols, int 
 #pragma unroll
     for (int j = 0; j < kItems; ++j) {
       const int col = t + j * kGroup;
-      v[j] = col < cols ? Io16<T>::load(row[col]) : fill;
+      v[j] = col < cols ? ld_ro16(row + col) : fill;
     }
   }
 }
@@ -158,7 +171,7 @@ __global__ void __launch_bounds__(kBlock)
       }
     } else {
       const int col = t + j * kGroup;
-      w[0] = col < hidden ? Io16<T>::load(weight[col]) : 0.0f;
+      w[0] = col < hidden ? ld_ro16(weight + col) : 0.0f;
     }
 #pragma unroll
     for (int i = 0; i < kW; ++i) v[kW * j + i] = v[kW * j + i] * inverse_rms * w[i];
