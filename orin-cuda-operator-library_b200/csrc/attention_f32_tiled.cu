@@ -215,6 +215,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int j = 0; j < 4; ++j) s2[r][j] = 0;
+    // Causal: a warp whose 16 rows (8tr.. for its two tr) all precede this
+    // tile's first key sees none of it -- its S and PV loops are skipped
+    // (warp-uniform); the mask below then gives P = 0 and an unchanged max.
+    const bool warp_masked = causal && q0 + 16 * (tid >> 5) + 15 < k0;
+    if (!warp_masked)
 #pragma unroll 8
     for (int d = 0; d < D; ++d) {
       const ulonglong2 qa = *reinterpret_cast<const ulonglong2*>(&qt[d * Cfg::kQPitch + tr * 8]);
@@ -287,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     // O += P V over this tile's keys.
-    const int key_count = min(kBN, seq - k0);
+    const int key_count = warp_masked ? 0 : min(kBN, seq - k0);
 #pragma unroll 4
     for (int j = 0; j < key_count; ++j) {
       const float4 pa = *reinterpret_cast<const float4*>(&pt[j * Cfg::kPPitch + tr * 8]);
